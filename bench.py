@@ -1,0 +1,450 @@
+"""Benchmark of the B200 paged-KV attention path (one JSON line on rank 0).
+
+Default workload (``--workload decode``, the BASELINE config 2 the headline
+metric is quoted on): per GPU, 64 requests whose context after this step's
+token is drawn uniformly from 1024..8192, Qwen3-4B attention heads (32 query /
+8 KV, head_dim 128), bf16, 128-token pages with seeded shuffled page tables,
+inputs N(0,1) with QK-norm and RoPE theta 1e6. One step = scatter the step's
+new K/V into the pool (kernel a) + split-KV decode attention (kernel c) for
+one layer. The KV read per step (about 1.2 GB) is far larger than the 126 MB
+L2, so no flush is needed between steps.
+
+``--workload prefill`` times config 3 (8 requests x 512-token chunk on a
+prefix U[0, 4096]); ``--workload longdecode`` times config 5 (512 requests x
+32768-token context in groups of 16 sharing a 4096-token prefix, split across
+ranks by group).
+
+Multi-GPU: one process per GPU (torchrun), each rank owns its own pool and
+requests; there is no collective on the data path. Timing is by CUDA events,
+max over ranks (NCCL all_reduce of the elapsed times only).
+
+``--impl reference`` times the CPU oracle (a NumPy restatement of hayate's
+paged attention, the reference being pure Python/PyTorch with no compiled
+path) on a bounded sample of the same workload with every host thread.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "hayate-exp_b200"))
+sys.path.insert(0, ROOT)
+
+PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["decode", "prefill", "longdecode"], default="decode")
+    ap.add_argument("--split-tokens", type=int, default=0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    try:
+        with open(PEAKS_PATH) as f:
+            peaks = json.load(f)
+        return peaks, "measured"
+    except (OSError, ValueError):
+        return FALLBACK_PEAKS, "fallback"
+
+
+# ---------------------------------------------------------------------------- workloads
+def decode_lengths(seed: int, batch: int = 64, lo: int = 1024, hi: int = 8192):
+    """Context lengths after the step's token; the cached history is one less."""
+    rng = np.random.RandomState(seed)
+    return [int(n) for n in rng.randint(lo, hi + 1, size=batch)]
+
+
+def prefill_prefixes(seed: int, batch: int = 8, hi: int = 4096):
+    rng = np.random.RandomState(seed)
+    return [int(n) for n in rng.randint(0, hi + 1, size=batch)]
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled in the background (read-only)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int, period_ms: int = 50):
+        self.gpu_index = gpu_index
+        self.period_ms = period_ms
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu_index), "-lms", str(self.period_ms)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------- distributed
+def dist_setup(args):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------- decode (cfg 2)
+def build_decode(rank: int, split_tokens: int):
+    import torch
+
+    from hayate_b200 import PagedKVCacheManager
+    from hayate_b200 import workloads as W
+
+    ctx = decode_lengths(1000 + rank)
+    hist = [n - 1 for n in ctx]
+    pages = sum(math.ceil(n / 128) for n in ctx) + 8
+    manager = PagedKVCacheManager(1, 8, 128, pages * 128, 128, len(ctx), torch.bfloat16, "cuda")
+    manager.split_tokens = split_tokens
+    W.shuffle_free_pages(manager, 1000 + rank)
+    gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
+    handles = [manager.allocate() for _ in ctx]
+    for h, n in zip(handles, hist):
+        W.fill_history(manager, h, n, gen)
+    q, k, v = W.step_inputs(manager, handles, 1, 32, gen)
+    return manager, handles, ctx, q, k, v
+
+
+def run_decode(args, world, rank, local, peaks, peak_kind):
+    import torch
+
+    from hayate_b200 import ops
+
+    manager, handles, ctx, q, k, v = build_decode(rank, args.split_tokens)
+    kv_bytes = sum(ctx) * 8 * 128 * 2 * 2           # K and V rows read by attention
+    scatter_bytes = 2 * 2 * len(ctx) * 8 * 128 * 2    # read + write of the new K and V rows
+    q_out_bytes = 2 * len(ctx) * 32 * 128 * 2
+    step_bytes = kv_bytes + scatter_bytes + q_out_bytes
+    batch = manager.begin_batch(handles, 1)
+    out = torch.empty((len(ctx), 1, 32, 128), dtype=q.dtype, device="cuda").transpose(1, 2)
+    ws = manager.workspace_for(len(ctx), 1, 32, batch.max_kv_len)
+
+    def step(attn_events=None):
+        ops.kv_scatter(k, v, manager.k_cache, manager.v_cache, 0, batch.page_table,
+                       batch.cache_lens_i32, 128, error_word=manager.error_word)
+        if attn_events is not None:
+            attn_events[0].record()
+        ops.paged_attention(q, manager.k_cache, manager.v_cache, 0, batch.page_table,
+                            batch.cache_lens_i32, 128, batch.max_kv_len, out=out, workspace=ws,
+                            error_word=manager.error_word, split_tokens=args.split_tokens)
+        if attn_events is not None:
+            attn_events[1].record()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    manager.check_device_errors()
+
+    attn = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record()
+        for i in range(args.steps):
+            step(attn[i])
+        end.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    ms_local = start.elapsed_time(end)
+    attn_ms = sum(a.elapsed_time(b) for a, b in attn) / args.steps
+    manager.check_device_errors()
+    ms_total = max_over_ranks(ms_local, world)
+    total_bytes = sum_over_ranks(float(step_bytes), world)
+    value = total_bytes * args.steps / (ms_total / 1e3) / 1e9
+    achieved = kv_bytes / (attn_ms / 1e3) / 1e9
+    peak = peaks["hbm_gbs"]
+
+    result = {
+        "metric": "decode attn HBM GB/s (% of peak)",
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_total / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) q/k/v, QK-norm + RoPE theta 1e6 at true positions, shuffled page tables",
+        "config": {
+            "workload": "config 2: bf16 paged decode sweep (scatter + split-KV decode attention, 1 layer)",
+            "requests_per_gpu": len(ctx), "kv_len": "U[1024, 8192]", "mean_kv_len": round(float(np.mean(ctx)), 1),
+            "query_heads": 32, "kv_heads": 8, "head_dim": 128, "page_size": 128,
+            "l2": "inputs larger than L2 (KV read per step ~%.2f GB > 126 MB)" % (kv_bytes / 1e9),
+            "parallelism": f"request-parallel x{world} (own pool per GPU, no data-path collective)",
+            "split_tokens": args.split_tokens or "auto",
+        },
+        "step_bytes_per_gpu": step_bytes,
+        "attention_only": {"ms": round(attn_ms, 4), "GB_s": round(achieved, 1),
+                           "frac_of_peak": round(achieved / peak, 4)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
+                     "nominal_frac_8TBs": round(achieved / 8000.0, 4), "traffic": None,
+                     "kernel": "decode_attention_kernel (split-KV decode)"},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if not args.no_e2e:
+        result["e2e"] = decode_e2e(args, world, manager, handles, ctx, q, k, v, step_bytes)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline_decode(manager, batch, q, ctx)
+    return result
+
+
+def decode_e2e(args, world, manager, handles, ctx, q, k, v, step_bytes):
+    """Same step through the public API with host buffers: H2D inputs, D2H output."""
+    import torch
+
+    q_h = q.detach().cpu().pin_memory()
+    k_h = k.detach().cpu().pin_memory()
+    v_h = v.detach().cpu().pin_memory()
+    out_h = torch.empty((len(ctx), 32, 1, 128), dtype=q.dtype).pin_memory()
+
+    def step():
+        batch = manager.begin_batch(handles, 1)               # H2D: page table + lengths
+        qd = q_h.to("cuda", non_blocking=True)
+        kd = k_h.to("cuda", non_blocking=True)
+        vd = v_h.to("cuda", non_blocking=True)
+        batch.write_layer(0, kd, vd)
+        o = batch.attend_layer(qd, 0)
+        out_h.copy_(o, non_blocking=True)                     # D2H of the step's result
+        return batch
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    meta_bytes = (3 * len(ctx) + len(ctx) * max(len(h.pages) for h in handles)) * 4
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(args.steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    total = sum_over_ranks(float(step_bytes), world)
+    manager.check_device_errors()
+    return {"value": round(total * args.steps / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
+            "ms_per_step": round(ms / args.steps, 4),
+            "h2d_bytes_per_step": int(q_h.numel() * 2 + k_h.numel() * 2 + v_h.numel() * 2 + meta_bytes),
+            "d2h_bytes_per_step": int(out_h.numel() * 2),
+            "path": "PagedKVCacheManager.begin_batch -> write_layer -> attend_layer, pinned host buffers"}
+
+
+def cpu_threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+
+
+def cpu_baseline_decode(manager, batch, q, ctx, budget_s: float = 15.0):
+    """The oracle (NumPy restatement of the reference path) on a bounded sample of requests."""
+    import oracle
+    from threadpoolctl import threadpool_limits
+
+    threads = cpu_threads()
+    kp = manager.k_cache.float().cpu().numpy()
+    vp = manager.v_cache.float().cpu().numpy()
+    table = batch.page_table.cpu().numpy().astype(np.int64)
+    lens = batch.cache_lens.cpu().numpy()
+    qn = q.float().cpu().numpy()
+    done, nbytes = 0, 0
+    t0 = time.perf_counter()
+    with threadpool_limits(limits=threads):
+        while time.perf_counter() - t0 < budget_s and done < len(ctx):
+            oracle.paged_attention(qn, kp, vp, 0, table, lens, 128, requests=[done])
+            nbytes += ctx[done] * 8 * 128 * 2 * 2
+            done += 1
+    secs = time.perf_counter() - t0
+    return {"value": round(nbytes / secs / 1e9, 3), "unit": "GB/s", "cores": threads,
+            "kind": "port",
+            "sample": f"{done} of {len(ctx)} requests of the config-2 batch (fp32 NumPy oracle, "
+                      f"bf16-rounded inputs), {secs:.1f} s"}
+
+
+# ---------------------------------------------------------------------------- reference arm
+def run_reference(args, world, rank):
+    """CPU oracle on the host cores, same metric/unit/config as the GPU arm (rank 0 only)."""
+    if rank != 0:
+        return None
+    import oracle
+    from threadpoolctl import threadpool_limits
+
+    threads = cpu_threads()
+    ctx = decode_lengths(1000)
+    rng = np.random.RandomState(7)
+    step_bytes_per_req = [n * 8 * 128 * 2 * 2 for n in ctx]
+    # each step: one request of the batch (rotating), its own pool slice, K/V scatter + attention
+    pools = {}
+    t_total, b_total = 0.0, 0
+    with threadpool_limits(limits=threads):
+        for i in range(args.warmup + args.steps):
+            r = i % len(ctx)
+            n = ctx[r]
+            if r not in pools:
+                pages = math.ceil(n / 128)
+                kp = rng.standard_normal((1, 1, 8, pages * 128, 128)).astype(np.float32)
+                vp = rng.standard_normal((1, 1, 8, pages * 128, 128)).astype(np.float32)
+                table = rng.permutation(pages)[None].astype(np.int64)
+                qn = rng.standard_normal((1, 32, 1, 128)).astype(np.float32)
+                kn = rng.standard_normal((1, 8, 1, 128)).astype(np.float32)
+                pools = {r: (kp, vp, table, qn, kn)}
+            kp, vp, table, qn, kn = pools[r]
+            t0 = time.perf_counter()
+            oracle.kv_scatter(kp, vp, 0, kn, kn, table, np.array([n - 1]), 128)
+            oracle.paged_attention(qn, kp, vp, 0, table, np.array([n - 1]), 128)
+            dt = time.perf_counter() - t0
+            if i >= args.warmup:
+                t_total += dt
+                b_total += step_bytes_per_req[r]
+    value = b_total / t_total / 1e9
+    return {
+        "impl": "reference",
+        "metric": "decode attn HBM GB/s (% of peak)", "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(t_total / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic N(0,1), config-2 lengths",
+        "config": {"workload": "config 2: paged decode sweep; each step = one request of the 64-request batch",
+                   "query_heads": 32, "kv_heads": 8, "head_dim": 128, "page_size": 128},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": "one request per step, rotating through the config-2 batch"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+# ---------------------------------------------------------------------------- main
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        result = run_reference(args, world, rank)
+        if result is not None:
+            print(json.dumps(result), flush=True)
+        return
+    import torch
+
+    world, rank, local = dist_setup(args)
+    peaks, peak_kind = load_peaks()
+    if args.workload == "decode":
+        result = run_decode(args, world, rank, local, peaks, peak_kind)
+    else:
+        raise SystemExit(f"workload {args.workload} is not built yet")
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    del torch
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,443 @@
+// C ABI of hayate_b200 (declared in include/hayate_b200.h).
+//
+// Host-side argument checks, TMA tensor maps over the KV pools, workspace
+// sizing and the choice between the decode, prefill and CUDA-core kernels.
+// Every entry point only enqueues work on the caller's stream.
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t err, const char* what) {
+  return fail(HYT_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
+}
+
+bool is_pow2(int64_t v) { return v > 0 && (v & (v - 1)) == 0; }
+
+int log2_int(int64_t v) {
+  int s = 0;
+  while ((int64_t(1) << s) < v) ++s;
+  return s;
+}
+
+int elem_bytes(int dtype) { return dtype == HYT_DTYPE_F32 ? 4 : 2; }
+
+// ------------------------------------------------------------------ tensor maps
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult status;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &status) ==
+            cudaSuccess &&
+        status == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    }
+  });
+  return fn;
+}
+
+struct MapKey {
+  const void* ptr;
+  int dtype, head_dim, box_rows;
+  int64_t capacity, planes;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && dtype == o.dtype && head_dim == o.head_dim && box_rows == o.box_rows &&
+           capacity == o.capacity && planes == o.planes;
+  }
+};
+
+struct MapCache {
+  static constexpr int kEntries = 32;
+  MapKey keys[kEntries];
+  CUtensorMap maps[kEntries];
+  bool used[kEntries] = {};
+  int next = 0;
+  std::mutex mu;
+};
+
+MapCache& map_cache() {
+  static MapCache cache;
+  return cache;
+}
+
+// Tensor map over a whole pool viewed as [planes = layers * H_kv][capacity][head_dim],
+// box = [box_rows tokens x 64 dims], 128-byte swizzle (the layout the kernels index).
+int pool_tensor_map(const void* pool, int dtype, int head_dim, int64_t capacity, int64_t planes,
+                    int box_rows, CUtensorMap* out) {
+  MapKey key{pool, dtype, head_dim, box_rows, capacity, planes};
+  MapCache& cache = map_cache();
+  std::lock_guard<std::mutex> lock(cache.mu);
+  for (int i = 0; i < MapCache::kEntries; ++i) {
+    if (cache.used[i] && cache.keys[i] == key) {
+      *out = cache.maps[i];
+      return HYT_OK;
+    }
+  }
+  EncodeTiledFn encode = encode_fn();
+  if (encode == nullptr) return fail(HYT_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if (reinterpret_cast<uintptr_t>(pool) % 16)
+    return fail(HYT_ERR_INVALID, "KV pool base address must be 16-byte aligned for TMA");
+  const int eb = elem_bytes(dtype);
+  cuuint64_t dims[3] = {cuuint64_t(head_dim), cuuint64_t(capacity), cuuint64_t(planes)};
+  cuuint64_t strides[2] = {cuuint64_t(head_dim) * eb, cuuint64_t(capacity) * head_dim * eb};
+  cuuint32_t box[3] = {64, cuuint32_t(box_rows), 1};
+  cuuint32_t estrides[3] = {1, 1, 1};
+  CUtensorMap map;
+  CUresult res = encode(&map,
+                        dtype == HYT_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                               : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                        3, const_cast<void*>(pool), dims, strides, box, estrides,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (res != CUDA_SUCCESS)
+    return fail(HYT_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string(int(res)));
+  const int slot = cache.next;
+  cache.next = (cache.next + 1) % MapCache::kEntries;
+  cache.keys[slot] = key;
+  cache.maps[slot] = map;
+  cache.used[slot] = true;
+  *out = map;
+  return HYT_OK;
+}
+
+// ------------------------------------------------------------------ argument checks
+struct Geometry {
+  int32_t num_layers, layer;
+  int64_t capacity;
+  int32_t page_table_stride;
+  int32_t batch, query_len, num_q_heads, num_kv_heads, head_dim, page_size, dtype;
+};
+
+int check_geometry(const Geometry& g) {
+  if (g.batch < 1) return fail(HYT_ERR_INVALID, "batch must be positive");
+  if (g.query_len < 1) return fail(HYT_ERR_INVALID, "query_len must be positive");
+  if (g.num_kv_heads < 1 || g.num_q_heads < 1 || g.num_q_heads % g.num_kv_heads)
+    return fail(HYT_ERR_INVALID, "num_q_heads must be a positive multiple of num_kv_heads");
+  if (g.head_dim < 1) return fail(HYT_ERR_INVALID, "head_dim must be positive");
+  if (!is_pow2(g.page_size)) return fail(HYT_ERR_INVALID, "page_size must be a positive power of two");
+  if (g.capacity < g.page_size || g.capacity % g.page_size)
+    return fail(HYT_ERR_INVALID, "capacity_tokens must be a positive multiple of page_size");
+  if (g.capacity / g.page_size > INT32_MAX) return fail(HYT_ERR_INVALID, "too many pages");
+  if (g.num_layers < 1 || g.layer < 0 || g.layer >= g.num_layers)
+    return fail(HYT_ERR_INVALID, "layer must be within [0, num_layers)");
+  if (g.page_table_stride < 1) return fail(HYT_ERR_INVALID, "page_table_stride must be positive");
+  if (g.dtype != HYT_DTYPE_BF16 && g.dtype != HYT_DTYPE_F16 && g.dtype != HYT_DTYPE_F32)
+    return fail(HYT_ERR_INVALID, "unknown dtype");
+  return HYT_OK;
+}
+
+hyt::AttentionParams attention_params(const void* q, const int64_t* qs, const void* k_pool,
+                                      const void* v_pool, const Geometry& g,
+                                      const int32_t* page_table, const int32_t* cache_lens,
+                                      void* out, const int64_t* os, float scale,
+                                      int32_t* error_word) {
+  hyt::AttentionParams p;
+  p.q = q;
+  p.q_sb = qs[0];
+  p.q_sh = qs[1];
+  p.q_st = qs[2];
+  p.out = out;
+  p.o_sb = os[0];
+  p.o_sh = os[1];
+  p.o_st = os[2];
+  p.k_pool = k_pool;
+  p.v_pool = v_pool;
+  p.capacity = g.capacity;
+  p.num_layers = g.num_layers;
+  p.layer = g.layer;
+  p.page_table = page_table;
+  p.page_table_stride = g.page_table_stride;
+  p.cache_lens = cache_lens;
+  p.batch = g.batch;
+  p.query_len = g.query_len;
+  p.num_q_heads = g.num_q_heads;
+  p.num_kv_heads = g.num_kv_heads;
+  p.head_dim = g.head_dim;
+  p.page_shift = log2_int(g.page_size);
+  p.num_pages = int32_t(g.capacity / g.page_size);
+  p.scale = scale;
+  p.error_word = error_word;
+  return p;
+}
+
+int check_attention_pointers(const void* q, const int64_t* qs, const void* k_pool,
+                             const void* v_pool, const int32_t* page_table,
+                             const int32_t* cache_lens, const void* out, const int64_t* os) {
+  if (!q || !qs || !k_pool || !v_pool || !page_table || !cache_lens || !out || !os)
+    return fail(HYT_ERR_INVALID, "null pointer argument");
+  return HYT_OK;
+}
+
+// ------------------------------------------------------------------ decode sizing
+constexpr int64_t kB200Slots = 148 * 2;  // resident decode CTAs on one B200
+
+bool decode_eligible(const Geometry& g) {
+  return (g.dtype == HYT_DTYPE_BF16 || g.dtype == HYT_DTYPE_F16) && g.head_dim == 128 &&
+         g.page_size % 64 == 0 &&
+         (g.num_q_heads / g.num_kv_heads) * g.query_len <= hyt::kDecodeMaxRows;
+}
+
+int32_t decode_split_tokens(int32_t batch, int32_t num_kv_heads, int32_t max_kv_len,
+                            int32_t requested) {
+  const int64_t tiles_per_seq = (int64_t(max_kv_len) + 63) / 64;
+  int64_t split_tiles;
+  if (requested > 0) {
+    split_tiles = (int64_t(requested) + 63) / 64;
+  } else {
+    const int64_t total = int64_t(batch) * num_kv_heads * tiles_per_seq;
+    const int64_t target = 8 * kB200Slots;
+    split_tiles = (total + target - 1) / target;
+    if (split_tiles < 8) split_tiles = 8;
+  }
+  if (split_tiles > tiles_per_seq) split_tiles = tiles_per_seq;
+  if (split_tiles < 1) split_tiles = 1;
+  return int32_t(split_tiles * 64);
+}
+
+struct DecodeLayout {
+  int32_t split_tokens, max_splits, rows;
+  size_t counter_bytes, ml_bytes, o_bytes, total;
+};
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+DecodeLayout decode_layout(int32_t batch, int32_t query_len, int32_t num_q_heads,
+                           int32_t num_kv_heads, int32_t max_kv_len, int32_t split_tokens) {
+  DecodeLayout L;
+  L.split_tokens = decode_split_tokens(batch, num_kv_heads, max_kv_len, split_tokens);
+  L.max_splits = int32_t((int64_t(max_kv_len) + L.split_tokens - 1) / L.split_tokens);
+  L.rows = (num_q_heads / num_kv_heads) * query_len;
+  const size_t units = size_t(batch) * num_kv_heads;
+  if (L.max_splits <= 1) {
+    L.counter_bytes = L.ml_bytes = L.o_bytes = L.total = 0;
+    return L;
+  }
+  L.counter_bytes = align256(units * sizeof(int32_t));
+  L.ml_bytes = align256(units * L.max_splits * L.rows * 2 * sizeof(float));
+  L.o_bytes = units * L.max_splits * L.rows * 128 * sizeof(float);
+  L.total = L.counter_bytes + L.ml_bytes + L.o_bytes;
+  return L;
+}
+
+int launch_decode(const void* q, const int64_t* qs, const void* k_pool, const void* v_pool,
+                  const Geometry& g, const int32_t* page_table, const int32_t* cache_lens,
+                  void* out, const int64_t* os, float scale, int32_t max_kv_len,
+                  int32_t split_tokens, void* workspace, size_t workspace_bytes,
+                  int32_t* error_word, cudaStream_t stream) {
+  if (max_kv_len < g.query_len) return fail(HYT_ERR_INVALID, "max_kv_len must be >= query_len");
+  if (split_tokens < 0) return fail(HYT_ERR_INVALID, "split_tokens must be >= 0");
+  const DecodeLayout L = decode_layout(g.batch, g.query_len, g.num_q_heads, g.num_kv_heads,
+                                       max_kv_len, split_tokens);
+  if (L.max_splits > 65535) return fail(HYT_ERR_UNSUPPORTED, "too many splits for one launch");
+  if (g.batch > 65535 || g.num_kv_heads > 65535) return fail(HYT_ERR_UNSUPPORTED, "batch too large");
+  if (L.total > 0 && (workspace == nullptr || workspace_bytes < L.total))
+    return fail(HYT_ERR_WORKSPACE, "workspace missing or smaller than hyt_attention_workspace_bytes()");
+  CUtensorMap k_map, v_map;
+  const int64_t planes = int64_t(g.num_layers) * g.num_kv_heads;
+  int rc = pool_tensor_map(k_pool, g.dtype, g.head_dim, g.capacity, planes, 64, &k_map);
+  if (rc != HYT_OK) return rc;
+  rc = pool_tensor_map(v_pool, g.dtype, g.head_dim, g.capacity, planes, 64, &v_map);
+  if (rc != HYT_OK) return rc;
+  hyt::AttentionParams p = attention_params(q, qs, k_pool, v_pool, g, page_table, cache_lens,
+                                            out, os, scale, error_word);
+  hyt::DecodeLaunch d;
+  d.split_tokens = L.split_tokens;
+  d.max_splits = L.max_splits;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  d.ws_counter = L.total ? reinterpret_cast<int32_t*>(ws) : nullptr;
+  d.ws_ml = L.total ? reinterpret_cast<float*>(ws + L.counter_bytes) : nullptr;
+  d.ws_o = L.total ? reinterpret_cast<float*>(ws + L.counter_bytes + L.ml_bytes) : nullptr;
+  cudaError_t err = hyt::run_decode_attention(p, d, k_map, v_map, g.dtype, stream);
+  if (err != cudaSuccess) return cuda_fail(err, "decode attention launch");
+  return HYT_OK;
+}
+
+int launch_generic(const void* q, const int64_t* qs, const void* k_pool, const void* v_pool,
+                   const Geometry& g, const int32_t* page_table, const int32_t* cache_lens,
+                   void* out, const int64_t* os, float scale, int32_t* error_word,
+                   cudaStream_t stream) {
+  if (g.head_dim % 8 || g.head_dim > 256)
+    return fail(HYT_ERR_UNSUPPORTED, "head_dim must be a multiple of 8 and at most 256");
+  hyt::AttentionParams p = attention_params(q, qs, k_pool, v_pool, g, page_table, cache_lens,
+                                            out, os, scale, error_word);
+  cudaError_t err = hyt::run_generic_attention(p, g.dtype, stream);
+  if (err != cudaSuccess) return cuda_fail(err, "generic attention launch");
+  return HYT_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* hyt_last_error(void) { return g_last_error.c_str(); }
+
+int hyt_version(void) { return 100; }
+
+int hyt_kv_scatter(const void* k_new, const void* v_new, const int64_t* new_strides,
+                   void* k_pool, void* v_pool, int32_t num_layers, int32_t layer,
+                   int64_t capacity_tokens, const int32_t* page_table,
+                   int32_t page_table_stride, const int32_t* cache_lens, int32_t batch,
+                   int32_t query_len, int32_t num_kv_heads, int32_t head_dim,
+                   int32_t page_size, int32_t dtype, int32_t* error_word, void* stream) {
+  g_last_error.clear();
+  if (!k_new || !v_new || !new_strides || !k_pool || !v_pool || !page_table || !cache_lens)
+    return fail(HYT_ERR_INVALID, "null pointer argument");
+  Geometry g{num_layers, layer, capacity_tokens, page_table_stride, batch, query_len,
+             num_kv_heads, num_kv_heads, head_dim, page_size, dtype};
+  int rc = check_geometry(g);
+  if (rc != HYT_OK) return rc;
+  hyt::ScatterParams p;
+  p.k_new = static_cast<const uint8_t*>(k_new);
+  p.v_new = static_cast<const uint8_t*>(v_new);
+  p.k_sb = new_strides[0];
+  p.k_sh = new_strides[1];
+  p.k_st = new_strides[2];
+  p.v_sb = new_strides[3];
+  p.v_sh = new_strides[4];
+  p.v_st = new_strides[5];
+  p.k_pool = static_cast<uint8_t*>(k_pool);
+  p.v_pool = static_cast<uint8_t*>(v_pool);
+  p.layer_offset = int64_t(layer) * num_kv_heads * capacity_tokens * head_dim;
+  p.capacity = capacity_tokens;
+  p.page_table = page_table;
+  p.page_table_stride = page_table_stride;
+  p.cache_lens = cache_lens;
+  p.batch = batch;
+  p.query_len = query_len;
+  p.heads = num_kv_heads;
+  p.head_dim = head_dim;
+  p.page_shift = log2_int(page_size);
+  p.num_pages = int32_t(capacity_tokens / page_size);
+  p.error_word = error_word;
+  cudaError_t err = hyt::run_kv_scatter(p, elem_bytes(dtype), static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "kv scatter launch");
+  return HYT_OK;
+}
+
+int hyt_generic_attention(const void* q, const int64_t* q_strides, const void* k_pool,
+                          const void* v_pool, int32_t num_layers, int32_t layer,
+                          int64_t capacity_tokens, const int32_t* page_table,
+                          int32_t page_table_stride, const int32_t* cache_lens, void* out,
+                          const int64_t* out_strides, int32_t batch, int32_t query_len,
+                          int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                          int32_t page_size, int32_t dtype, float scale,
+                          int32_t* error_word, void* stream) {
+  g_last_error.clear();
+  int rc = check_attention_pointers(q, q_strides, k_pool, v_pool, page_table, cache_lens, out,
+                                    out_strides);
+  if (rc != HYT_OK) return rc;
+  Geometry g{num_layers, layer, capacity_tokens, page_table_stride, batch, query_len,
+             num_q_heads, num_kv_heads, head_dim, page_size, dtype};
+  rc = check_geometry(g);
+  if (rc != HYT_OK) return rc;
+  return launch_generic(q, q_strides, k_pool, v_pool, g, page_table, cache_lens, out,
+                        out_strides, scale, error_word, static_cast<cudaStream_t>(stream));
+}
+
+int hyt_decode_attention(const void* q, const int64_t* q_strides, const void* k_pool,
+                         const void* v_pool, int32_t num_layers, int32_t layer,
+                         int64_t capacity_tokens, const int32_t* page_table,
+                         int32_t page_table_stride, const int32_t* cache_lens, void* out,
+                         const int64_t* out_strides, int32_t batch, int32_t query_len,
+                         int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                         int32_t page_size, int32_t dtype, float scale, int32_t max_kv_len,
+                         int32_t split_tokens, void* workspace, size_t workspace_bytes,
+                         int32_t* error_word, void* stream) {
+  g_last_error.clear();
+  int rc = check_attention_pointers(q, q_strides, k_pool, v_pool, page_table, cache_lens, out,
+                                    out_strides);
+  if (rc != HYT_OK) return rc;
+  Geometry g{num_layers, layer, capacity_tokens, page_table_stride, batch, query_len,
+             num_q_heads, num_kv_heads, head_dim, page_size, dtype};
+  rc = check_geometry(g);
+  if (rc != HYT_OK) return rc;
+  if (!decode_eligible(g))
+    return fail(HYT_ERR_UNSUPPORTED,
+                "decode kernel needs bf16/f16, head_dim 128, page_size % 64 == 0 and "
+                "group * query_len <= 16");
+  return launch_decode(q, q_strides, k_pool, v_pool, g, page_table, cache_lens, out,
+                       out_strides, scale, max_kv_len, split_tokens, workspace, workspace_bytes,
+                       error_word, static_cast<cudaStream_t>(stream));
+}
+
+int hyt_prefill_attention(const void* q, const int64_t* q_strides, const void* k_pool,
+                          const void* v_pool, int32_t num_layers, int32_t layer,
+                          int64_t capacity_tokens, const int32_t* page_table,
+                          int32_t page_table_stride, const int32_t* cache_lens, void* out,
+                          const int64_t* out_strides, int32_t batch, int32_t query_len,
+                          int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                          int32_t page_size, int32_t dtype, float scale, int32_t max_kv_len,
+                          int32_t* error_word, void* stream) {
+  g_last_error.clear();
+  (void)q; (void)q_strides; (void)k_pool; (void)v_pool; (void)num_layers; (void)layer;
+  (void)capacity_tokens; (void)page_table; (void)page_table_stride; (void)cache_lens;
+  (void)out; (void)out_strides; (void)batch; (void)query_len; (void)num_q_heads;
+  (void)num_kv_heads; (void)head_dim; (void)page_size; (void)dtype; (void)scale;
+  (void)max_kv_len; (void)error_word; (void)stream;
+  return fail(HYT_ERR_UNSUPPORTED, "prefill kernel not built yet");
+}
+
+int hyt_paged_attention(const void* q, const int64_t* q_strides, const void* k_pool,
+                        const void* v_pool, int32_t num_layers, int32_t layer,
+                        int64_t capacity_tokens, const int32_t* page_table,
+                        int32_t page_table_stride, const int32_t* cache_lens, void* out,
+                        const int64_t* out_strides, int32_t batch, int32_t query_len,
+                        int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                        int32_t page_size, int32_t dtype, float scale, int32_t max_kv_len,
+                        int32_t split_tokens, void* workspace, size_t workspace_bytes,
+                        int32_t* error_word, void* stream) {
+  g_last_error.clear();
+  int rc = check_attention_pointers(q, q_strides, k_pool, v_pool, page_table, cache_lens, out,
+                                    out_strides);
+  if (rc != HYT_OK) return rc;
+  Geometry g{num_layers, layer, capacity_tokens, page_table_stride, batch, query_len,
+             num_q_heads, num_kv_heads, head_dim, page_size, dtype};
+  rc = check_geometry(g);
+  if (rc != HYT_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (decode_eligible(g))
+    return launch_decode(q, q_strides, k_pool, v_pool, g, page_table, cache_lens, out,
+                         out_strides, scale, max_kv_len, split_tokens, workspace,
+                         workspace_bytes, error_word, s);
+  return launch_generic(q, q_strides, k_pool, v_pool, g, page_table, cache_lens, out,
+                        out_strides, scale, error_word, s);
+}
+
+size_t hyt_attention_workspace_bytes(int32_t batch, int32_t query_len, int32_t num_q_heads,
+                                     int32_t num_kv_heads, int32_t head_dim,
+                                     int32_t max_kv_len, int32_t split_tokens, int32_t dtype) {
+  if (batch < 1 || query_len < 1 || num_kv_heads < 1 || num_q_heads < 1 ||
+      num_q_heads % num_kv_heads || max_kv_len < 1 || split_tokens < 0)
+    return 0;
+  Geometry g{1, 0, 128, 1, batch, query_len, num_q_heads, num_kv_heads, head_dim, 128, dtype};
+  if (!decode_eligible(g)) return 0;
+  return decode_layout(batch, query_len, num_q_heads, num_kv_heads, max_kv_len, split_tokens).total;
+}
+
+int hyt_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (workspace_bytes == 0) return HYT_OK;
+  if (workspace == nullptr) return fail(HYT_ERR_INVALID, "null workspace");
+  cudaError_t err = cudaMemsetAsync(workspace, 0, workspace_bytes, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "workspace memset");
+  return HYT_OK;
+}
+
+}  // extern "C"

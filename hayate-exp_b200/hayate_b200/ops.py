@@ -1,0 +1,158 @@
+"""Tensor-level wrappers of the native kernels (device tensors in, device tensors out).
+
+Each function checks devices, dtypes and layouts, hands raw pointers and
+element strides to the C ABI and raises ``RuntimeError`` with the library's
+message if the call is refused. All launches go on the current CUDA stream.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.bfloat16: _lib.HYT_DTYPE_BF16, torch.float16: _lib.HYT_DTYPE_F16,
+           torch.float32: _lib.HYT_DTYPE_F32}
+
+KERNELS = ("auto", "decode", "prefill", "generic")
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPES[dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dtype}; expected bf16, f16 or f32") from None
+
+
+def _require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if not t.is_cuda:
+            raise RuntimeError("hayate_b200 kernels run on CUDA tensors only (no CPU fallback)")
+
+
+def _stream_ptr() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _bht_strides(t: torch.Tensor, name: str) -> tuple[int, int, int]:
+    if t.dim() != 4:
+        raise ValueError(f"{name} must be [batch, heads, tokens, head_dim]")
+    if t.stride(3) != 1 and t.size(3) > 1:
+        raise ValueError(f"{name} must have a contiguous last dimension")
+    return t.stride(0), t.stride(1), t.stride(2)
+
+
+def _pool_geometry(k_pool: torch.Tensor, v_pool: torch.Tensor) -> tuple[int, int, int, int]:
+    if k_pool.dim() != 5 or k_pool.size(1) != 1:
+        raise ValueError("pools must be [num_layers, 1, num_kv_heads, capacity_tokens, head_dim]")
+    if k_pool.shape != v_pool.shape or k_pool.dtype != v_pool.dtype:
+        raise ValueError("K and V pools must have the same shape and dtype")
+    if not (k_pool.is_contiguous() and v_pool.is_contiguous()):
+        raise ValueError("pools must be contiguous")
+    num_layers, _, heads, capacity, head_dim = k_pool.shape
+    return num_layers, heads, capacity, head_dim
+
+
+def _table_args(page_table: torch.Tensor, cache_lens: torch.Tensor, batch: int):
+    if page_table.dtype != torch.int32 or cache_lens.dtype != torch.int32:
+        raise TypeError("page_table and cache_lens must be int32")
+    if page_table.dim() != 2 or page_table.size(0) != batch or page_table.stride(1) != 1:
+        raise ValueError("page_table must be [batch, pages] with contiguous rows")
+    if cache_lens.numel() != batch or not cache_lens.is_contiguous():
+        raise ValueError("cache_lens must be a contiguous [batch] tensor")
+    return page_table.stride(0)
+
+
+def kv_scatter(k_new: torch.Tensor, v_new: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+               layer: int, page_table: torch.Tensor, cache_lens: torch.Tensor, page_size: int,
+               error_word: torch.Tensor | None = None) -> None:
+    """Kernel (a): write ``[B, H_kv, T, D]`` K/V into the pools at ``page_table`` slots."""
+    _require_cuda(k_new, v_new, k_pool, v_pool, page_table, cache_lens)
+    num_layers, heads, capacity, head_dim = _pool_geometry(k_pool, v_pool)
+    if k_new.shape != v_new.shape or k_new.dtype != k_pool.dtype or v_new.dtype != k_pool.dtype:
+        raise ValueError("k/v must share one shape and the pool dtype")
+    batch, h, query_len, d = k_new.shape
+    if h != heads or d != head_dim:
+        raise ValueError("k/v heads and head_dim must match the pool")
+    strides = _lib.int64_array(_bht_strides(k_new, "k") + _bht_strides(v_new, "v"))
+    pts = _table_args(page_table, cache_lens, batch)
+    rc = _lib.lib().hyt_kv_scatter(
+        k_new.data_ptr(), v_new.data_ptr(), strides, k_pool.data_ptr(), v_pool.data_ptr(),
+        num_layers, layer, capacity, page_table.data_ptr(), pts, cache_lens.data_ptr(), batch,
+        query_len, heads, head_dim, page_size, dtype_code(k_pool.dtype), _ptr(error_word),
+        _stream_ptr())
+    _lib.check(rc, "hyt_kv_scatter")
+
+
+def attention_workspace_bytes(batch: int, query_len: int, num_q_heads: int, num_kv_heads: int,
+                              head_dim: int, max_kv_len: int, dtype: torch.dtype,
+                              split_tokens: int = 0) -> int:
+    return int(_lib.lib().hyt_attention_workspace_bytes(batch, query_len, num_q_heads, num_kv_heads,
+                                                        head_dim, max_kv_len, split_tokens,
+                                                        dtype_code(dtype)))
+
+
+def new_workspace(nbytes: int, device) -> torch.Tensor:
+    """A zeroed byte workspace (the kernels keep its counter area zero between calls)."""
+    return torch.zeros(max(nbytes, 1), dtype=torch.uint8, device=device)
+
+
+def paged_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, layer: int,
+                    page_table: torch.Tensor, cache_lens: torch.Tensor, page_size: int,
+                    max_kv_len: int, scale: float | None = None, out: torch.Tensor | None = None,
+                    workspace: torch.Tensor | None = None, error_word: torch.Tensor | None = None,
+                    kernel: str = "auto", split_tokens: int = 0) -> torch.Tensor:
+    """Causal GQA attention of ``q`` ``[B, H_q, T, D]`` over the paged pools.
+
+    ``max_kv_len`` must be at least ``cache_lens[b] + T`` for every row.
+    ``kernel`` pins one kernel instead of the library's choice.
+    """
+    if kernel not in KERNELS:
+        raise ValueError(f"kernel must be one of {KERNELS}")
+    _require_cuda(q, k_pool, v_pool, page_table, cache_lens)
+    num_layers, num_kv_heads, capacity, head_dim = _pool_geometry(k_pool, v_pool)
+    batch, num_q_heads, query_len, d = q.shape
+    if d != head_dim or q.dtype != k_pool.dtype:
+        raise ValueError("q must match the pool's head_dim and dtype")
+    if out is None:
+        # [B, T, H, D] memory viewed as [B, H, T, D]: the caller's transpose(1, 2) is then free
+        out = torch.empty((batch, query_len, num_q_heads, head_dim), dtype=q.dtype,
+                          device=q.device).transpose(1, 2)
+    if out.shape != q.shape or out.dtype != q.dtype:
+        raise ValueError("out must match q")
+    qs = _lib.int64_array(_bht_strides(q, "q"))
+    os_ = _lib.int64_array(_bht_strides(out, "out"))
+    pts = _table_args(page_table, cache_lens, batch)
+    scale = 1.0 / math.sqrt(head_dim) if scale is None else float(scale)
+    lib = _lib.lib()
+    common = (q.data_ptr(), qs, k_pool.data_ptr(), v_pool.data_ptr(), num_layers, layer, capacity,
+              page_table.data_ptr(), pts, cache_lens.data_ptr(), out.data_ptr(), os_, batch,
+              query_len, num_q_heads, num_kv_heads, head_dim, page_size, dtype_code(q.dtype), scale)
+    stream = _stream_ptr()
+    if kernel == "generic":
+        rc = lib.hyt_generic_attention(*common, _ptr(error_word), stream)
+    elif kernel == "prefill":
+        rc = lib.hyt_prefill_attention(*common, max_kv_len, _ptr(error_word), stream)
+    else:
+        need = attention_workspace_bytes(batch, query_len, num_q_heads, num_kv_heads, head_dim,
+                                         max_kv_len, q.dtype, split_tokens)
+        if need and (workspace is None or workspace.numel() < need):
+            raise RuntimeError(f"attention needs a zeroed workspace of {need} bytes")
+        ws_ptr = _ptr(workspace) if need else None
+        ws_bytes = workspace.numel() if (need and workspace is not None) else 0
+        fn = lib.hyt_decode_attention if kernel == "decode" else lib.hyt_paged_attention
+        rc = fn(*common, max_kv_len, split_tokens, ws_ptr, ws_bytes, _ptr(error_word), stream)
+    _lib.check(rc, f"paged attention ({kernel})")
+    return out
+
+
+def read_device_errors(error_word: torch.Tensor) -> list[str]:
+    """Decode (and synchronise on) a device error word; empty if no kernel refused anything."""
+    value = int(error_word.item())
+    return [msg for bit, msg in _lib.DEVICE_ERRORS.items() if value & bit]

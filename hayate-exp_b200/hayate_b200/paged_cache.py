@@ -1,0 +1,380 @@
+"""Drop-in paged KV pool for hayate, backed by the hayate_b200 CUDA kernels.
+
+Same public surface as ``hayate/engine/paged_cache.py``:
+
+* ``PagedCacheHandle`` (``:23-30``), ``PagedKVCacheManager`` (``:74-315``) with
+  ``allocate``/``reserve``/``allocate_for_request``/``import_cache``/``truncate``/
+  ``snapshot``/``release``/``begin_batch``/``commit_batch`` and the same
+  arguments, free-list order and exceptions (``ValueError``, ``RuntimeError``,
+  ``MemoryError``);
+* ``begin_batch`` returns a ``PagedKVBatch`` exposing ``write_layer(layer, k, v)``,
+  ``attend_layer(q, layer)``, ``cache_lens`` (int64, read by the model to place
+  RoPE positions), ``page_table`` and ``page_size`` (``:33-71``).
+
+What changes underneath:
+
+* ``write_layer`` is one launch of the scatter kernel and ``attend_layer`` one
+  launch of the decode, prefill or CUDA-core attention kernel. There is no
+  block mask and no ``physical_to_logical`` table: the kernels walk the page
+  table and apply the causal rule ``key <= cache_len + t`` themselves.
+* The per-step metadata (int64 and int32 lengths plus an int32 page table only
+  as wide as the batch's longest request) is packed into one host buffer and
+  uploaded with a single host-to-device copy, instead of one copy per request.
+* Pages carry reference counts, so ``share`` can alias a prefix's physical
+  pages into another request (prefix-cache page sharing). ``release`` and
+  ``truncate`` decrement; a page returns to the free list at zero. A write that
+  would land in a page someone else still holds copies that page first.
+* Pools start zeroed (the reference uses ``torch.empty``): tiles that straddle
+  a request's last token read finite bytes, so masked keys contribute exactly 0.
+* ``attend_layer`` returns ``[B, H_q, T, D]`` backed by ``[B, T, H_q, D]``
+  memory, so the attention module's ``transpose(1, 2).reshape(...)`` is free.
+
+Pools may live on the CPU for the bookkeeping API (allocation, import,
+snapshot); ``write_layer``/``attend_layer`` run on CUDA only and raise otherwise.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Sequence
+
+import numpy as np
+import torch
+
+from . import ops
+from .cache import Cache
+
+MIN_KV_PAGE_SIZE = 128  # hayate/engine/constants.py:27 (FlexAttention block size floor)
+
+
+@dataclass
+class PagedCacheHandle:
+    """One request's physical KV pages and logical cache length."""
+
+    slot: int
+    pages: list[int] = field(default_factory=list)
+    length: int = 0
+    released: bool = False
+
+
+class _MetaUploader:
+    """Asynchronous host-to-device upload of a step's packed metadata.
+
+    A small ring of pinned host buffers, each guarded by the CUDA event of its
+    last copy, so ``begin_batch`` never blocks on the GPU queue.
+    """
+
+    def __init__(self, device: torch.device, slots: int = 4):
+        self.device = device
+        self.buffers: list[torch.Tensor | None] = [None] * slots
+        self.events: list[torch.cuda.Event | None] = [None] * slots
+        self.index = 0
+
+    def upload(self, host: np.ndarray) -> torch.Tensor:
+        if self.device.type != "cuda":
+            return torch.from_numpy(host.copy()).to(self.device)
+        i = self.index
+        self.index = (i + 1) % len(self.buffers)
+        if self.events[i] is not None:
+            self.events[i].synchronize()
+        buf = self.buffers[i]
+        if buf is None or buf.numel() < host.size:
+            buf = torch.empty(max(host.size, 4096), dtype=torch.int32, pin_memory=True)
+            self.buffers[i] = buf
+        staged = buf[: host.size]
+        staged.numpy()[:] = host
+        dev = torch.empty(host.size, dtype=torch.int32, device=self.device)
+        dev.copy_(staged, non_blocking=True)
+        event = torch.cuda.Event()
+        event.record()
+        self.events[i] = event
+        return dev
+
+
+class PagedKVBatch:
+    """Per-step metadata shared by every layer of one forward pass."""
+
+    __slots__ = ("k_cache", "v_cache", "page_table", "cache_lens", "page_size", "query_len",
+                 "max_kv_len", "cache_lens_i32", "_manager", "_meta")
+
+    def __init__(self, manager, page_table, cache_lens, cache_lens_i32, query_len, max_kv_len, meta):
+        self.k_cache = manager.k_cache
+        self.v_cache = manager.v_cache
+        self.page_table = page_table
+        self.cache_lens = cache_lens
+        self.cache_lens_i32 = cache_lens_i32
+        self.page_size = manager.page_size
+        self.query_len = query_len
+        self.max_kv_len = max_kv_len
+        self._manager = manager
+        self._meta = meta  # keeps the uploaded buffer alive while kernels read it
+
+    def write_layer(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor) -> None:
+        """Scatter the step's new K/V ``[B, H_kv, T, D]`` into this layer's pages."""
+        if k.shape[2] != self.query_len or v.shape != k.shape:
+            raise ValueError("k and v must be [batch, kv_heads, query_len, head_dim]")
+        if k.stride(-1) != 1:
+            k = k.contiguous()
+        if v.stride(-1) != 1:
+            v = v.contiguous()
+        ops.kv_scatter(k, v, self.k_cache, self.v_cache, layer_idx, self.page_table,
+                       self.cache_lens_i32, self.page_size, error_word=self._manager.error_word)
+
+    def attend_layer(self, q: torch.Tensor, layer_idx: int) -> torch.Tensor:
+        """Causal GQA attention of ``q`` ``[B, H_q, T, D]`` over this layer's paged K/V."""
+        if q.stride(-1) != 1:
+            q = q.contiguous()
+        manager = self._manager
+        workspace = manager.workspace_for(q.shape[0], self.query_len, q.shape[1], self.max_kv_len)
+        return ops.paged_attention(q, self.k_cache, self.v_cache, layer_idx, self.page_table,
+                                   self.cache_lens_i32, self.page_size, self.max_kv_len,
+                                   workspace=workspace, error_word=manager.error_word,
+                                   kernel=manager.kernel, split_tokens=manager.split_tokens)
+
+
+class PagedKVCacheManager:
+    """Allocate fixed-size, reference-counted pages from shared K/V pools."""
+
+    def __init__(self, num_layers: int, num_kv_heads: int, head_dim: int, max_cache_tokens: int,
+                 page_size: int, max_requests: int, dtype: torch.dtype,
+                 device: torch.device | str):
+        if max_cache_tokens < 1:
+            raise ValueError("max_cache_tokens must be positive")
+        if page_size < 1 or page_size & (page_size - 1):
+            raise ValueError("page_size must be a positive power of two")
+        if max_requests < 1:
+            raise ValueError("max_requests must be positive")
+        self.page_size = page_size
+        self.num_pages = math.ceil(max_cache_tokens / page_size)
+        self.capacity_tokens = self.num_pages * page_size
+        self.max_requests = max_requests
+        self.num_layers = num_layers
+        self.num_kv_heads = num_kv_heads
+        self.head_dim = head_dim
+        self.device = torch.device(device)
+        # stacks popped from the end: the lowest slot / page id comes out first
+        self._free_slots = list(range(max_requests - 1, -1, -1))
+        self._free_pages = list(range(self.num_pages - 1, -1, -1))
+        self._page_refs = np.zeros(self.num_pages, dtype=np.int32)
+        shape = (num_layers, 1, num_kv_heads, self.capacity_tokens, head_dim)
+        self.k_cache = torch.zeros(shape, dtype=dtype, device=self.device)
+        self.v_cache = torch.zeros_like(self.k_cache)
+        self.error_word = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._workspace: torch.Tensor | None = None
+        self._uploader = _MetaUploader(self.device)
+        self.kernel = "auto"     # pin a kernel ("decode", "prefill", "generic") for testing
+        self.split_tokens = 0    # 0 lets the library pick the decode split size
+
+    # ------------------------------------------------------------------ pages
+    def _take_pages(self, count: int) -> list[int]:
+        pages = [self._free_pages.pop() for _ in range(count)]
+        self._page_refs[pages] = 1
+        return pages
+
+    def _drop_pages(self, pages: Sequence[int]) -> None:
+        for page in pages:
+            self._page_refs[page] -= 1
+            if self._page_refs[page] == 0:
+                self._free_pages.append(page)
+
+    def page_refcount(self, page: int) -> int:
+        return int(self._page_refs[page])
+
+    def allocate(self) -> PagedCacheHandle:
+        """Reserve a request slot without allocating KV pages yet."""
+        if not self._free_slots:
+            raise MemoryError(f"paged cache supports at most {self.max_requests} active requests")
+        return PagedCacheHandle(slot=self._free_slots.pop())
+
+    def reserve(self, handle: PagedCacheHandle, required_tokens: int) -> None:
+        """Allocate enough pages for ``required_tokens`` logical positions."""
+        if handle.released:
+            raise RuntimeError("cannot reserve pages for a released cache handle")
+        if required_tokens < 0:
+            raise ValueError("required_tokens must be non-negative")
+        if required_tokens > self.capacity_tokens:
+            raise MemoryError(
+                f"request needs {required_tokens} cache tokens, but the paged cache "
+                f"capacity is {self.capacity_tokens} tokens")
+        missing = math.ceil(required_tokens / self.page_size) - len(handle.pages)
+        if missing <= 0:
+            return
+        if len(self._free_pages) < missing:
+            raise MemoryError(
+                f"paged KV cache is full: need {missing} additional pages, "
+                f"but only {len(self._free_pages)} remain")
+        handle.pages.extend(self._take_pages(missing))
+
+    def share(self, source: PagedCacheHandle, num_tokens: int) -> PagedCacheHandle:
+        """New handle whose first ``num_tokens`` alias ``source``'s physical pages.
+
+        No K/V is copied: the pages' reference counts go up. The new request then
+        appends into pages of its own (a write into a still-shared page copies it).
+        """
+        if source.released:
+            raise RuntimeError("cannot share pages of a released cache handle")
+        if num_tokens < 0 or num_tokens > source.length:
+            raise ValueError("shared length must be within the source's cache length")
+        handle = self.allocate()
+        pages = source.pages[: math.ceil(num_tokens / self.page_size)]
+        for page in pages:
+            self._page_refs[page] += 1
+        handle.pages = list(pages)
+        handle.length = num_tokens
+        return handle
+
+    def _make_writable(self, handle: PagedCacheHandle, first: int, last: int) -> None:
+        """Copy-on-write every page holding logical positions ``first..last`` that is shared."""
+        if last < first:
+            return
+        for logical in range(first // self.page_size, last // self.page_size + 1):
+            old = handle.pages[logical]
+            if self._page_refs[old] <= 1:
+                continue
+            if not self._free_pages:
+                raise MemoryError("paged KV cache is full: no page left to copy a shared page")
+            new = self._take_pages(1)[0]
+            size = self.page_size
+            for pool in (self.k_cache, self.v_cache):
+                pool[:, :, :, new * size:(new + 1) * size].copy_(pool[:, :, :, old * size:(old + 1) * size])
+            self._drop_pages([old])
+            handle.pages[logical] = new
+
+    def allocate_for_request(self, cache=None) -> PagedCacheHandle:
+        """Allocate a request handle and optionally import a contiguous prefix."""
+        handle = self.allocate()
+        try:
+            if cache is not None and cache.length:
+                self.import_cache(handle, cache)
+        except Exception:
+            self.release(handle)
+            raise
+        return handle
+
+    def import_cache(self, handle: PagedCacheHandle, cache) -> None:
+        """Copy a contiguous ``[layers, H_kv, tokens, D]`` prefix into the request's pages."""
+        if cache.k is None or cache.v is None:
+            return
+        length = cache.length
+        self.reserve(handle, length)
+        self._make_writable(handle, 0, length - 1)
+        slots = self._physical_positions(handle, length)
+        for layer in range(cache.k.shape[0]):
+            for pool, src in ((self.k_cache, cache.k), (self.v_cache, cache.v)):
+                pool[layer, 0].index_copy_(
+                    1, slots, src[layer, :, :length].to(device=pool.device, dtype=pool.dtype))
+        handle.length = length
+
+    def truncate(self, handle: PagedCacheHandle, length: int) -> None:
+        """Shorten a cache and drop whole pages beyond its new end."""
+        if handle.released:
+            raise RuntimeError("cannot truncate a released cache handle")
+        if length < 0 or length > handle.length:
+            raise ValueError("truncate length must be within the current cache length")
+        keep = math.ceil(length / self.page_size)
+        dropped = handle.pages[keep:]
+        handle.pages = handle.pages[:keep]
+        self._drop_pages(dropped)
+        handle.length = length
+
+    def snapshot(self, handle: PagedCacheHandle, length: int | None = None) -> Cache:
+        """Gather a compact ``[layers, H_kv, length, D]`` copy of a request's cache."""
+        if handle.released:
+            raise RuntimeError("cannot snapshot a released cache handle")
+        n = handle.length if length is None else length
+        if n < 0 or n > handle.length:
+            raise ValueError("snapshot length must be within the current cache length")
+        slots = self._physical_positions(handle, n)
+        k = self.k_cache[:, 0].index_select(2, slots).contiguous()
+        v = self.v_cache[:, 0].index_select(2, slots).contiguous()
+        return Cache.from_tensors(k, v)
+
+    def release(self, handle: PagedCacheHandle) -> None:
+        """Drop a request's pages and return its slot."""
+        if handle.released:
+            return
+        self._drop_pages(handle.pages)
+        handle.pages.clear()
+        handle.length = 0
+        handle.released = True
+        self._free_slots.append(handle.slot)
+
+    # ------------------------------------------------------------------ steps
+    def begin_batch(self, handles: Sequence[PagedCacheHandle], query_len: int) -> PagedKVBatch:
+        """Reserve append space and upload one step's page table and lengths."""
+        if not handles:
+            raise ValueError("cannot build paged cache metadata for an empty batch")
+        if query_len < 1:
+            raise ValueError("query_len must be positive")
+        if any(handle.released for handle in handles):
+            raise RuntimeError("cannot use a released cache handle in an attention batch")
+        if len({id(handle) for handle in handles}) != len(handles):
+            raise ValueError("an attention batch cannot contain the same cache handle twice")
+        if self.page_size < MIN_KV_PAGE_SIZE:
+            raise ValueError(f"page_size must be at least {MIN_KV_PAGE_SIZE} tokens")
+        lengths = [handle.length for handle in handles]
+        kv_lengths = [length + query_len for length in lengths]
+        if max(kv_lengths) > self.capacity_tokens:
+            raise MemoryError(
+                f"request needs more than the paged cache capacity of {self.capacity_tokens} tokens")
+        extra = sum(max(0, math.ceil(n / self.page_size) - len(h.pages))
+                    for h, n in zip(handles, kv_lengths))
+        if extra > len(self._free_pages):
+            raise MemoryError(
+                f"paged KV cache is full: batch needs {extra} additional pages, "
+                f"but only {len(self._free_pages)} remain")
+        for handle, target in zip(handles, kv_lengths):
+            self.reserve(handle, target)
+            self._make_writable(handle, handle.length, handle.length + query_len - 1)
+
+        batch = len(handles)
+        width = max(len(handle.pages) for handle in handles)
+        # one int32 upload: [cache_lens as int64 (2B words) | cache_lens int32 (B) | table (B x W)]
+        host = np.full(3 * batch + batch * width, -1, dtype=np.int32)
+        host[: 2 * batch].view(np.int64)[:] = lengths
+        host[2 * batch: 3 * batch] = lengths
+        table = host[3 * batch:].reshape(batch, width)
+        for row, handle in enumerate(handles):
+            table[row, : len(handle.pages)] = handle.pages
+        meta = self._uploader.upload(host)
+        return PagedKVBatch(self, meta[3 * batch:].view(batch, width), meta[: 2 * batch].view(torch.int64),
+                            meta[2 * batch: 3 * batch], query_len, max(kv_lengths), meta)
+
+    def commit_batch(self, handles: Sequence[PagedCacheHandle], query_len: int) -> None:
+        """Advance logical lengths after every layer wrote the step's K/V."""
+        for handle in handles:
+            if handle.released:
+                raise RuntimeError("cannot commit a released cache handle")
+            if handle.length + query_len > len(handle.pages) * self.page_size:
+                raise RuntimeError("paged cache append space was not reserved")
+            handle.length += query_len
+
+    # ------------------------------------------------------------------ helpers
+    def workspace_for(self, batch: int, query_len: int, num_q_heads: int, max_kv_len: int):
+        """Grow-only zeroed workspace for the split-KV decode kernel (None if not needed)."""
+        need = ops.attention_workspace_bytes(batch, query_len, num_q_heads, self.num_kv_heads,
+                                             self.head_dim, max_kv_len, self.k_cache.dtype,
+                                             self.split_tokens)
+        if need == 0:
+            return None
+        if self._workspace is None or self._workspace.numel() < need:
+            self._workspace = ops.new_workspace(need, self.device)
+        return self._workspace
+
+    def check_device_errors(self) -> None:
+        """Synchronise and raise if a kernel refused a page id or length since the last check."""
+        problems = ops.read_device_errors(self.error_word)
+        if problems:
+            self.error_word.zero_()
+            if self._workspace is not None:
+                self._workspace.zero_()
+            raise RuntimeError("paged attention kernels refused input: " + "; ".join(problems))
+
+    def _physical_positions(self, handle: PagedCacheHandle, length: int) -> torch.Tensor:
+        if length == 0:
+            return torch.empty(0, dtype=torch.long, device=self.device)
+        logical = np.arange(length, dtype=np.int64)
+        pages = np.asarray(handle.pages, dtype=np.int64)[logical // self.page_size]
+        slots = pages * self.page_size + logical % self.page_size
+        return torch.from_numpy(slots).to(self.device)

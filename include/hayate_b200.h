@@ -1,0 +1,145 @@
+/*
+ * hayate_b200 — C ABI of the B200 paged-KV attention path.
+ *
+ * Drop-in for hayate's paged attention seam: the Python side keeps the
+ * reference's PagedKVCacheManager / PagedKVBatch API and calls these entry
+ * points with raw device pointers (no torch types cross this boundary).
+ *
+ * Conventions shared by every entry point:
+ *  - Pools are the reference's layout, [num_layers, 1, num_kv_heads,
+ *    capacity_tokens, head_dim], contiguous, one for K and one for V
+ *    (hayate/engine/paged_cache.py:104-109).
+ *  - page_table is int32 [batch, page_table_stride] on the device; row b lists
+ *    request b's physical page ids in logical order. cache_lens is int32 [batch]
+ *    on the device: the tokens cached BEFORE this step. Every request appends
+ *    query_len tokens, so kv_len[b] = cache_lens[b] + query_len
+ *    (paged_cache.py:216-217).
+ *  - q/out/k_new/v_new are [batch, heads, query_len, head_dim] with the last
+ *    dimension contiguous; the other three strides are passed in ELEMENTS as
+ *    {stride_b, stride_h, stride_t}, so the strided views hayate's attention
+ *    module produces (hayate/model/attention.py:66-71) need no copy.
+ *  - dtype: HYT_DTYPE_BF16 / F16 / F32 for every tensor of the call.
+ *  - stream is a cudaStream_t (NULL = legacy default stream). Calls only
+ *    enqueue work; none of them synchronises the host.
+ *  - error_word (nullable) is a device int32 the kernels OR error bits into
+ *    when they meet a page id or length they refuse to use; the offending
+ *    access is skipped, never performed. Host-side argument errors are
+ *    returned as negative codes with a message in hyt_last_error().
+ */
+#ifndef HAYATE_B200_H
+#define HAYATE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  HYT_OK = 0,
+  HYT_ERR_INVALID = -1,     /* bad argument (null pointer, negative size, ...) */
+  HYT_ERR_UNSUPPORTED = -2, /* valid but not served by this build (dtype/shape) */
+  HYT_ERR_CUDA = -3,        /* a CUDA runtime/driver call failed */
+  HYT_ERR_WORKSPACE = -4    /* workspace missing or too small */
+};
+
+enum { HYT_DTYPE_BF16 = 0, HYT_DTYPE_F16 = 1, HYT_DTYPE_F32 = 2 };
+
+/* Device error bits written into error_word. */
+enum {
+  HYT_DEVERR_PAGE_RANGE = 1,   /* page id outside [0, capacity_tokens / page_size) */
+  HYT_DEVERR_TABLE_RANGE = 2,  /* kv_len needs more pages than page_table_stride */
+  HYT_DEVERR_SPLIT_RANGE = 4,  /* kv_len > max_kv_len given at launch */
+  HYT_DEVERR_WAIT_TIMEOUT = 8  /* a bounded pipeline wait gave up */
+};
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* hyt_last_error(void);
+
+/* ABI version of this library (major * 100 + minor). */
+int hyt_version(void);
+
+/*
+ * Page-table KV scatter.
+ * Replaces PagedKVBatch.write_layer (hayate/engine/paged_cache.py:44-60):
+ * token t of row b goes to slot page_table[b][(cache_lens[b]+t)/P]*P +
+ * (cache_lens[b]+t)%P of pool[layer, 0, h, :, :], for K and V in one launch.
+ * new_strides = {k_b, k_h, k_t, v_b, v_h, v_t} in elements.
+ */
+int hyt_kv_scatter(const void* k_new, const void* v_new, const int64_t* new_strides,
+                   void* k_pool, void* v_pool, int32_t num_layers, int32_t layer,
+                   int64_t capacity_tokens, const int32_t* page_table,
+                   int32_t page_table_stride, const int32_t* cache_lens, int32_t batch,
+                   int32_t query_len, int32_t num_kv_heads, int32_t head_dim,
+                   int32_t page_size, int32_t dtype, int32_t* error_word, void* stream);
+
+/*
+ * Paged causal GQA attention, any supported shape.
+ * Replaces PagedKVBatch.attend_layer (hayate/engine/paged_cache.py:62-71) with
+ * the reference's mask (paged_cache.py:266-271): query t of row b sees logical
+ * keys 0 .. cache_lens[b] + t. Query head h reads KV head h / (H_q / H_kv).
+ * Dispatches to the split-KV decode kernel (query_len * group <= 16,
+ * bf16/f16, head_dim 128), the tcgen05 chunked-prefill kernel (bf16/f16,
+ * head_dim 128, larger chunks) or the CUDA-core kernel (any other shape, f32).
+ * q_strides/out_strides = {b, h, t} in elements. max_kv_len bounds
+ * cache_lens[b] + query_len over the batch (sizes the split grid).
+ * workspace: see hyt_attention_workspace_bytes; the counter area at its start
+ * must be zero before the first use (hyt_workspace_init) and is left zero.
+ */
+int hyt_paged_attention(const void* q, const int64_t* q_strides, const void* k_pool,
+                        const void* v_pool, int32_t num_layers, int32_t layer,
+                        int64_t capacity_tokens, const int32_t* page_table,
+                        int32_t page_table_stride, const int32_t* cache_lens, void* out,
+                        const int64_t* out_strides, int32_t batch, int32_t query_len,
+                        int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                        int32_t page_size, int32_t dtype, float scale, int32_t max_kv_len,
+                        int32_t split_tokens, void* workspace, size_t workspace_bytes,
+                        int32_t* error_word, void* stream);
+
+/* Split-KV decode kernel only (query_len * (H_q / H_kv) <= 16, bf16/f16, D = 128).
+ * split_tokens: tokens per split, a multiple of 64; 0 picks one for this GPU. */
+int hyt_decode_attention(const void* q, const int64_t* q_strides, const void* k_pool,
+                         const void* v_pool, int32_t num_layers, int32_t layer,
+                         int64_t capacity_tokens, const int32_t* page_table,
+                         int32_t page_table_stride, const int32_t* cache_lens, void* out,
+                         const int64_t* out_strides, int32_t batch, int32_t query_len,
+                         int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                         int32_t page_size, int32_t dtype, float scale, int32_t max_kv_len,
+                         int32_t split_tokens, void* workspace, size_t workspace_bytes,
+                         int32_t* error_word, void* stream);
+
+/* tcgen05/TMEM chunked-prefill kernel only (bf16/f16, head_dim 128). */
+int hyt_prefill_attention(const void* q, const int64_t* q_strides, const void* k_pool,
+                          const void* v_pool, int32_t num_layers, int32_t layer,
+                          int64_t capacity_tokens, const int32_t* page_table,
+                          int32_t page_table_stride, const int32_t* cache_lens, void* out,
+                          const int64_t* out_strides, int32_t batch, int32_t query_len,
+                          int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                          int32_t page_size, int32_t dtype, float scale, int32_t max_kv_len,
+                          int32_t* error_word, void* stream);
+
+/* CUDA-core kernel only (any dtype, head_dim a multiple of 8 up to 256). */
+int hyt_generic_attention(const void* q, const int64_t* q_strides, const void* k_pool,
+                          const void* v_pool, int32_t num_layers, int32_t layer,
+                          int64_t capacity_tokens, const int32_t* page_table,
+                          int32_t page_table_stride, const int32_t* cache_lens, void* out,
+                          const int64_t* out_strides, int32_t batch, int32_t query_len,
+                          int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                          int32_t page_size, int32_t dtype, float scale,
+                          int32_t* error_word, void* stream);
+
+/* Workspace bytes hyt_paged_attention / hyt_decode_attention need for these sizes
+ * (0 when the dispatched kernel needs none). split_tokens as in the call. */
+size_t hyt_attention_workspace_bytes(int32_t batch, int32_t query_len, int32_t num_q_heads,
+                                     int32_t num_kv_heads, int32_t head_dim,
+                                     int32_t max_kv_len, int32_t split_tokens, int32_t dtype);
+
+/* Zero a workspace's counter area (enqueued on stream). */
+int hyt_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HAYATE_B200_H */

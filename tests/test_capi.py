@@ -1,0 +1,138 @@
+"""The C ABI library loads, exports what include/hayate_b200.h declares, and
+refuses bad arguments on the host (no GPU needed: every case returns before
+any CUDA call)."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from hayate_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
+                      "hayate_b200.h")
+
+
+def declared_functions() -> list[str]:
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(hyt_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    names = declared_functions()
+    assert len(names) >= 9
+    for name in names:
+        assert hasattr(lib, name), name
+    # the Python binding types every declared function
+    assert set(names) == set(_lib.SIGNATURES)
+
+
+def test_version_and_error_string():
+    lib = _lib.lib()
+    assert lib.hyt_version() == 100
+    assert lib.hyt_last_error() == b""
+
+
+def _scatter_args(**overrides):
+    strides = _lib.int64_array([0] * 6)
+    args = dict(k_new=1, v_new=1, strides=strides, k_pool=1, v_pool=1, num_layers=1, layer=0,
+                capacity=1024, page_table=1, pts=8, cache_lens=1, batch=1, query_len=1, heads=8,
+                head_dim=128, page_size=128, dtype=0, err=None, stream=None)
+    args.update(overrides)
+    return list(args.values())
+
+
+@pytest.mark.parametrize("bad, message", [
+    (dict(k_new=None), "null pointer"),
+    (dict(batch=0), "batch"),
+    (dict(query_len=0), "query_len"),
+    (dict(page_size=96), "power of two"),
+    (dict(capacity=1000), "multiple of page_size"),
+    (dict(layer=1), "layer"),
+    (dict(dtype=7), "dtype"),
+])
+def test_scatter_rejects_bad_arguments(bad, message):
+    lib = _lib.lib()
+    rc = lib.hyt_kv_scatter(*_scatter_args(**bad))
+    assert rc == -1
+    assert message in lib.hyt_last_error().decode()
+
+
+def _attention_args(**overrides):
+    s = _lib.int64_array([0, 0, 0])
+    args = dict(q=1, qs=s, k_pool=1, v_pool=1, num_layers=1, layer=0, capacity=4096,
+                page_table=1, pts=32, cache_lens=1, out=1, os=s, batch=2, query_len=1,
+                hq=32, hkv=8, head_dim=128, page_size=128, dtype=0, scale=0.088,
+                max_kv_len=4096, split_tokens=0, ws=None, ws_bytes=0, err=None, stream=None)
+    args.update(overrides)
+    return list(args.values())
+
+
+@pytest.mark.parametrize("bad, code, message", [
+    (dict(q=None), -1, "null pointer"),
+    (dict(hq=30), -1, "multiple of num_kv_heads"),
+    (dict(max_kv_len=0), -1, "max_kv_len"),
+    (dict(split_tokens=-64), -1, "split_tokens"),
+    (dict(max_kv_len=8192, ws=None), -4, "workspace"),
+])
+def test_attention_rejects_bad_arguments(bad, code, message):
+    lib = _lib.lib()
+    rc = lib.hyt_paged_attention(*_attention_args(**bad))
+    assert rc == code
+    assert message in lib.hyt_last_error().decode()
+
+
+def test_decode_entry_refuses_unsupported_shape():
+    lib = _lib.lib()
+    rc = lib.hyt_decode_attention(*_attention_args(head_dim=64))
+    assert rc == -2
+    assert "head_dim 128" in lib.hyt_last_error().decode()
+
+
+def test_generic_entry_refuses_unsupported_head_dim():
+    lib = _lib.lib()
+    args = _attention_args(head_dim=12)
+    # the generic entry point has no split/workspace arguments
+    args = args[:20] + args[24:]
+    rc = lib.hyt_generic_attention(*args)
+    assert rc == -2
+
+
+def test_workspace_bytes_formula():
+    lib = _lib.lib()
+    # one split per (request, head) needs no workspace
+    assert lib.hyt_attention_workspace_bytes(64, 1, 32, 8, 128, 512, 0, 0) == 0
+    # forced 1024-token splits over 8192 keys: 8 splits x 4 rows
+    units, splits, rows = 64 * 8, 8, 4
+    expect = (((units * 4) + 255) // 256 * 256 + ((units * splits * rows * 2 * 4) + 255) // 256 * 256
+              + units * splits * rows * 128 * 4)
+    assert lib.hyt_attention_workspace_bytes(64, 1, 32, 8, 128, 8192, 1024, 0) == expect
+    # f32 and head_dim 64 run on the CUDA-core kernel, which needs none
+    assert lib.hyt_attention_workspace_bytes(64, 1, 32, 8, 128, 8192, 1024, 2) == 0
+    assert lib.hyt_attention_workspace_bytes(64, 1, 32, 8, 64, 8192, 1024, 0) == 0
+
+
+def test_workspace_init_accepts_empty():
+    lib = _lib.lib()
+    assert lib.hyt_workspace_init(None, 0, None) == 0
+    assert lib.hyt_workspace_init(None, 16, None) == -1
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setenv("HAYATE_B200_LIB", str(tmp_path / "absent.so"))
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        _lib.lib()
+    monkeypatch.setattr(_lib, "_lib", None)
+
+
+def test_ctypes_types_are_plain():
+    # no torch types cross the boundary: every argument is a pointer or a scalar
+    for restype, argtypes in _lib.SIGNATURES.values():
+        for t in argtypes:
+            assert t in (ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t)

@@ -1,0 +1,184 @@
+"""GPU parity: the CUDA kernels against the reference's golden vectors and the oracle.
+
+Tolerances (max-abs on attention outputs): 2e-2 for bf16/f16, 1e-4 for f32.
+The scatter is compared bit for bit (SHA-256 of the whole pool).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from golden_util import CASES, load_golden, make_inputs, sha256_f32, shuffled_free_pages
+from hayate_b200 import Cache, PagedKVCacheManager, ops
+from hayate_b200 import workloads as W
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.bfloat16: 2e-2, torch.float16: 2e-2, torch.float32: 1e-4}
+
+
+def golden_run(case, dtype, kernel="auto", split_tokens=0):
+    golden = load_golden(case.name)
+    inputs = make_inputs(case)
+    manager = PagedKVCacheManager(case.num_layers, case.num_kv_heads, case.head_dim,
+                                  case.max_cache_tokens, case.page_size, case.batch, dtype, "cuda")
+    manager.kernel, manager.split_tokens = kernel, split_tokens
+    manager._free_pages = shuffled_free_pages(manager.num_pages, case.seed)
+    handles = []
+    for hk, hv in zip(inputs["hist_k"], inputs["hist_v"]):
+        cache = Cache.from_tensors(torch.from_numpy(hk), torch.from_numpy(hv)) if hk.shape[2] else None
+        handles.append(manager.allocate_for_request(cache))
+    batch = manager.begin_batch(handles, case.query_len)
+    dev = lambda a: torch.from_numpy(a).to("cuda", dtype)  # noqa: E731
+    batch.write_layer(case.layer, dev(inputs["k_new"]), dev(inputs["v_new"]))
+    out = batch.attend_layer(dev(inputs["q"]), case.layer)
+    torch.cuda.synchronize()
+    manager.check_device_errors()
+    return manager, out, golden
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32], ids=str)
+@pytest.mark.parametrize("case", CASES, ids=lambda c: c.name)
+def test_golden_case(case, dtype):
+    manager, out, golden = golden_run(case, dtype)
+    assert sha256_f32(manager.k_cache.float().cpu().numpy()) == str(golden["k_pool_sha256"])
+    assert sha256_f32(manager.v_cache.float().cpu().numpy()) == str(golden["v_pool_sha256"])
+    err = (out.float().cpu() - torch.from_numpy(golden["out"])).abs().max().item()
+    assert err <= TOL[dtype], err
+
+
+@pytest.mark.parametrize("kernel", ["generic", "decode"])
+def test_golden_decode_case_each_kernel(kernel):
+    case = [c for c in CASES if c.name == "qwen_decode"][0]
+    for split in (0, 64, 128):
+        _, out, golden = golden_run(case, torch.bfloat16, kernel=kernel, split_tokens=split)
+        err = (out.float().cpu() - torch.from_numpy(golden["out"])).abs().max().item()
+        assert err <= 2e-2, (split, err)
+
+
+def build_step(lengths, query_len, dtype=torch.bfloat16, seed=0, page_size=128, num_layers=1,
+               layer=0, slack_pages=2, strided=True):
+    """A manager holding synthetic histories, one step's inputs and its batch."""
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    pages = sum(math.ceil((n + query_len) / page_size) for n in lengths) + slack_pages
+    manager = PagedKVCacheManager(num_layers, 8, 128, pages * page_size, page_size,
+                                  len(lengths), dtype, "cuda")
+    W.shuffle_free_pages(manager, seed)
+    handles = [manager.allocate() for _ in lengths]
+    for h, n in zip(handles, lengths):
+        W.fill_history(manager, h, n, gen, layers=[layer])
+    q, k, v = W.step_inputs(manager, handles, query_len, 32, gen, strided=strided)
+    batch = manager.begin_batch(handles, query_len)
+    return manager, handles, batch, q, k, v
+
+
+def oracle_out(manager, batch, q, layer=0, requests=None):
+    kp = manager.k_cache.float().cpu().numpy()
+    vp = manager.v_cache.float().cpu().numpy()
+    table = batch.page_table.cpu().numpy().astype(np.int64)
+    lens = batch.cache_lens.cpu().numpy()
+    return oracle.paged_attention(q.float().cpu().numpy(), kp, vp, layer, table, lens,
+                                  manager.page_size, requests=requests)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=str)
+@pytest.mark.parametrize("query_len", [1, 2, 3, 4])
+@pytest.mark.parametrize("split", [0, 64, 192, 1024])
+def test_decode_kernel_matches_oracle(query_len, split, dtype):
+    lengths = [0, 1, 63, 64, 127, 128, 1000, 2431]
+    manager, _, batch, q, k, v = build_step(lengths, query_len, dtype=dtype, seed=query_len)
+    manager.kernel, manager.split_tokens = "decode", split
+    batch.write_layer(0, k, v)
+    out = batch.attend_layer(q, 0)
+    torch.cuda.synchronize()
+    manager.check_device_errors()
+    ref = oracle_out(manager, batch, q)
+    err = np.abs(out.float().cpu().numpy() - ref).max()
+    assert err <= 2e-2, err
+
+
+def test_decode_is_deterministic_and_leaves_counters_zero():
+    manager, _, batch, q, k, v = build_step([3000, 5000, 70], 1, seed=3)
+    manager.kernel, manager.split_tokens = "decode", 256
+    batch.write_layer(0, k, v)
+    first = batch.attend_layer(q, 0).clone()
+    second = batch.attend_layer(q, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(first, second)
+    ws = manager._workspace
+    assert ws is not None and int(ws[:256].view(torch.int32).abs().sum()) == 0
+
+
+def test_full_size_decode_sweep_config():
+    """Config 2 shapes (B=64, kv 1024..8192): decode vs the CUDA-core kernel, plus an oracle sample."""
+    rng = np.random.RandomState(0)
+    lengths = [int(n) - 1 for n in rng.randint(1024, 8193, size=64)]
+    manager, _, batch, q, k, v = build_step(lengths, 1, seed=11)
+    batch.write_layer(0, k, v)
+    out = batch.attend_layer(q, 0)
+    manager.kernel = "generic"
+    ref_gpu = batch.attend_layer(q, 0)
+    torch.cuda.synchronize()
+    manager.check_device_errors()
+    assert (out.float() - ref_gpu.float()).abs().max().item() <= 2e-2
+    sample = [0, 17, 63]
+    ref = oracle_out(manager, batch, q, requests=sample)
+    err = np.abs(out.float().cpu().numpy()[sample] - ref[sample]).max()
+    assert err <= 2e-2, err
+
+
+@pytest.mark.parametrize("query_len", [1, 7, 130])
+def test_generic_kernel_f32_matches_oracle(query_len):
+    manager, _, batch, q, k, v = build_step([0, 200, 513], query_len, dtype=torch.float32, seed=5)
+    batch.write_layer(0, k, v)
+    out = batch.attend_layer(q, 0)
+    torch.cuda.synchronize()
+    ref = oracle_out(manager, batch, q)
+    err = np.abs(out.cpu().numpy() - ref).max()
+    assert err <= 1e-4, err
+
+
+def test_scatter_contiguous_and_strided_inputs_agree():
+    lengths = [5, 300]
+    outs = []
+    for strided in (True, False):
+        manager, _, batch, q, k, v = build_step(lengths, 3, seed=9, strided=strided)
+        batch.write_layer(0, k, v)
+        torch.cuda.synchronize()
+        outs.append((manager.k_cache.clone(), manager.v_cache.clone()))
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
+def test_kernels_flag_bad_page_ids_without_touching_memory():
+    """A page id past the pool is refused by the kernels' own range checks (error word set)."""
+    manager, _, batch, q, k, v = build_step([300], 1, seed=2)
+    table = batch.page_table.clone()
+    table[0, 2] = manager.num_pages + 5  # the new token's page: refused before any access
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    before = manager.k_cache.clone()
+    ops.kv_scatter(k, v, manager.k_cache, manager.v_cache, 0, table, batch.cache_lens_i32,
+                   manager.page_size, error_word=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & 1 and torch.equal(before, manager.k_cache)
+    for kernel in ("decode", "generic"):
+        err.zero_()
+        ws = ops.new_workspace(ops.attention_workspace_bytes(1, 1, 32, 8, 128, 301, q.dtype, 64), "cuda")
+        ops.paged_attention(q, manager.k_cache, manager.v_cache, 0, table, batch.cache_lens_i32,
+                            manager.page_size, 301, workspace=ws, error_word=err, kernel=kernel,
+                            split_tokens=64)
+        torch.cuda.synchronize()
+        assert int(err.item()) & 1, kernel
+
+
+def test_attend_output_layout_is_transpose_friendly():
+    manager, _, batch, q, k, v = build_step([10, 20], 1, seed=1)
+    batch.write_layer(0, k, v)
+    out = batch.attend_layer(q, 0)
+    assert out.shape == q.shape
+    assert out.transpose(1, 2).is_contiguous()
