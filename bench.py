@@ -48,11 +48,12 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["decode", "prefill", "longdecode"], default="decode")
     ap.add_argument("--split-tokens", type=int, default=0)
+    ap.add_argument("--requests", type=int, default=64, help="decode requests per GPU (64 = config 2)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -188,13 +189,13 @@ def sum_over_ranks(value: float, world: int) -> float:
 
 
 # ---------------------------------------------------------------------------- decode (cfg 2)
-def build_decode(rank: int, split_tokens: int):
+def build_decode(rank: int, split_tokens: int, requests: int = 64):
     import torch
 
     from hayate_b200 import PagedKVCacheManager
     from hayate_b200 import workloads as W
 
-    ctx = decode_lengths(1000 + rank)
+    ctx = decode_lengths(1000 + rank, batch=requests)
     hist = [n - 1 for n in ctx]
     pages = sum(math.ceil(n / 128) for n in ctx) + 8
     manager = PagedKVCacheManager(1, 8, 128, pages * 128, 128, len(ctx), torch.bfloat16, "cuda")
@@ -213,7 +214,7 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
 
     from hayate_b200 import ops
 
-    manager, handles, ctx, q, k, v = build_decode(rank, args.split_tokens)
+    manager, handles, ctx, q, k, v = build_decode(rank, args.split_tokens, args.requests)
     kv_bytes = sum(ctx) * 8 * 128 * 2 * 2           # K and V rows read by attention
     scatter_bytes = 2 * 2 * len(ctx) * 8 * 128 * 2    # read + write of the new K and V rows
     q_out_bytes = 2 * len(ctx) * 32 * 128 * 2
@@ -343,7 +344,7 @@ def cpu_threads() -> int:
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
 
 
-def cpu_baseline_decode(manager, batch, q, ctx, budget_s: float = 15.0):
+def cpu_baseline_decode(manager, batch, q, ctx, budget_s: float = 10.0):
     """The oracle (NumPy restatement of the reference path) on a bounded sample of requests."""
     import oracle
     from threadpoolctl import threadpool_limits
@@ -357,15 +358,16 @@ def cpu_baseline_decode(manager, batch, q, ctx, budget_s: float = 15.0):
     done, nbytes = 0, 0
     t0 = time.perf_counter()
     with threadpool_limits(limits=threads):
-        while time.perf_counter() - t0 < budget_s and done < len(ctx):
-            oracle.paged_attention(qn, kp, vp, 0, table, lens, 128, requests=[done])
-            nbytes += ctx[done] * 8 * 128 * 2 * 2
+        while time.perf_counter() - t0 < budget_s:
+            r = done % len(ctx)
+            oracle.paged_attention(qn, kp, vp, 0, table, lens, 128, requests=[r])
+            nbytes += ctx[r] * 8 * 128 * 2 * 2
             done += 1
     secs = time.perf_counter() - t0
     return {"value": round(nbytes / secs / 1e9, 3), "unit": "GB/s", "cores": threads,
             "kind": "port",
-            "sample": f"{done} of {len(ctx)} requests of the config-2 batch (fp32 NumPy oracle, "
-                      f"bf16-rounded inputs), {secs:.1f} s"}
+            "sample": f"{done} request-attentions cycling over the {len(ctx)}-request config-2 batch "
+                      f"(fp32 NumPy oracle on the same bf16-rounded inputs), {secs:.1f} s"}
 
 
 # ---------------------------------------------------------------------------- reference arm
