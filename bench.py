@@ -56,6 +56,7 @@ def parse_args():
     ap.add_argument("--requests", type=int, default=64, help="decode requests per GPU (64 = config 2)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="headline workload only")
     return ap.parse_args()
 
 
@@ -370,6 +371,78 @@ def cpu_baseline_decode(manager, batch, q, ctx, budget_s: float = 10.0):
                       f"(fp32 NumPy oracle on the same bf16-rounded inputs), {secs:.1f} s"}
 
 
+# ---------------------------------------------------------------------------- prefill (cfg 3)
+def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=None):
+    """8 requests x 512-token chunk on prefixes U[0, 4096]; scatter + tcgen05 prefill attention."""
+    import torch
+
+    import oracle
+    from hayate_b200 import PagedKVCacheManager, ops
+    from hayate_b200 import workloads as W
+
+    steps = args.steps if steps is None else steps
+    warmup = args.warmup if warmup is None else warmup
+    T = 512
+    prefixes = prefill_prefixes(2000 + rank)
+    pages = sum(math.ceil((n + T) / 128) for n in prefixes) + 8
+    manager = PagedKVCacheManager(1, 8, 128, pages * 128, 128, len(prefixes), torch.bfloat16, "cuda")
+    W.shuffle_free_pages(manager, 2000 + rank)
+    gen = torch.Generator(device="cuda").manual_seed(2000 + rank)
+    handles = [manager.allocate() for _ in prefixes]
+    for h, n in zip(handles, prefixes):
+        W.fill_history(manager, h, n, gen)
+    q, k, v = W.step_inputs(manager, handles, T, 32, gen)
+    batch = manager.begin_batch(handles, T)
+    out = torch.empty((len(prefixes), T, 32, 128), dtype=q.dtype, device="cuda").transpose(1, 2)
+    flops = oracle.attention_flops(prefixes, T, 32, 128)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")  # > 126 MB L2
+
+    def step(ev=None):
+        ops.kv_scatter(k, v, manager.k_cache, manager.v_cache, 0, batch.page_table,
+                       batch.cache_lens_i32, 128, error_word=manager.error_word)
+        if ev is not None:
+            ev[1].record()
+        ops.paged_attention(q, manager.k_cache, manager.v_cache, 0, batch.page_table,
+                            batch.cache_lens_i32, 128, batch.max_kv_len, out=out,
+                            error_word=manager.error_word)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    manager.check_device_errors()
+    evs = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(steps)]
+    with ClockSampler(local) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        for i in range(steps):
+            flush.fill_(i & 0xFF)  # evict the step's inputs from L2 (outside the timed events)
+            evs[i][0].record()
+            step(evs[i])
+            evs[i][2].record()
+        torch.cuda.synchronize()
+        barrier(world)
+    manager.check_device_errors()
+    step_ms = sum(a.elapsed_time(c) for a, _, c in evs) / steps
+    attn_ms = sum(b.elapsed_time(c) for _, b, c in evs) / steps
+    step_ms = max_over_ranks(step_ms, world)
+    total_flops = sum_over_ranks(float(flops), world)
+    achieved = flops / (attn_ms / 1e3) / 1e12
+    return {
+        "workload": "config 3: bf16 chunked prefill, 8 requests x 512-token chunk on prefixes U[0, 4096]",
+        "prefixes": prefixes, "value": round(total_flops / (step_ms / 1e3) / 1e12, 1), "unit": "TFLOP/s",
+        "ms_per_step": round(step_ms, 4), "flops_per_step": flops,
+        "attention_only": {"ms": round(attn_ms, 4), "TFLOP_s": round(achieved, 1)},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
+                     "frac_of_sustained": round(achieved / peaks["bf16_tflops_sustained"], 4),
+                     "peak_source": f"{peak_kind} bf16_tflops (burst)", "traffic": None,
+                     "kernel": "prefill_attention_kernel (tcgen05 + TMEM)"},
+        "l2": "256 MB buffer written between timed steps (L2 flush); events bracket each step",
+        "gpu_launches": 2 * steps,
+        "clocks": clocks.summary(),
+    }
+
+
 # ---------------------------------------------------------------------------- reference arm
 def run_reference(args, world, rank):
     """CPU oracle on the host cores, same metric/unit/config as the GPU arm (rank 0 only)."""
@@ -437,6 +510,11 @@ def main():
     peaks, peak_kind = load_peaks()
     if args.workload == "decode":
         result = run_decode(args, world, rank, local, peaks, peak_kind)
+        if not args.no_extras:
+            # config 3 beside the headline (short: 50 timed steps)
+            result["prefill"] = run_prefill(args, world, rank, local, peaks, peak_kind, steps=50, warmup=5)
+    elif args.workload == "prefill":
+        result = run_prefill(args, world, rank, local, peaks, peak_kind)
     else:
         raise SystemExit(f"workload {args.workload} is not built yet")
     if rank == 0:

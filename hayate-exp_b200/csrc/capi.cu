@@ -269,6 +269,37 @@ int launch_decode(const void* q, const int64_t* qs, const void* k_pool, const vo
   return HYT_OK;
 }
 
+bool rows_16b_aligned(const void* ptr, const int64_t* strides) {
+  if (reinterpret_cast<uintptr_t>(ptr) % 16) return false;
+  for (int i = 0; i < 3; ++i)
+    if (strides[i] % 8) return false;  // 8 elements of 2 bytes
+  return true;
+}
+
+bool prefill_eligible(const Geometry& g, const void* q, const int64_t* qs, const void* out,
+                      const int64_t* os) {
+  return (g.dtype == HYT_DTYPE_BF16 || g.dtype == HYT_DTYPE_F16) && g.head_dim == 128 &&
+         g.page_size % 128 == 0 && rows_16b_aligned(q, qs) && rows_16b_aligned(out, os);
+}
+
+int launch_prefill(const void* q, const int64_t* qs, const void* k_pool, const void* v_pool,
+                   const Geometry& g, const int32_t* page_table, const int32_t* cache_lens,
+                   void* out, const int64_t* os, float scale, int32_t* error_word,
+                   cudaStream_t stream) {
+  if (g.batch > 65535 || g.num_q_heads > 65535) return fail(HYT_ERR_UNSUPPORTED, "batch too large");
+  CUtensorMap k_map, v_map;
+  const int64_t planes = int64_t(g.num_layers) * g.num_kv_heads;
+  int rc = pool_tensor_map(k_pool, g.dtype, g.head_dim, g.capacity, planes, 128, &k_map);
+  if (rc != HYT_OK) return rc;
+  rc = pool_tensor_map(v_pool, g.dtype, g.head_dim, g.capacity, planes, 128, &v_map);
+  if (rc != HYT_OK) return rc;
+  hyt::AttentionParams p = attention_params(q, qs, k_pool, v_pool, g, page_table, cache_lens,
+                                            out, os, scale, error_word);
+  cudaError_t err = hyt::run_prefill_attention(p, k_map, v_map, g.dtype, stream);
+  if (err != cudaSuccess) return cuda_fail(err, "prefill attention launch");
+  return HYT_OK;
+}
+
 int launch_generic(const void* q, const int64_t* qs, const void* k_pool, const void* v_pool,
                    const Geometry& g, const int32_t* page_table, const int32_t* cache_lens,
                    void* out, const int64_t* os, float scale, int32_t* error_word,
@@ -386,12 +417,20 @@ int hyt_prefill_attention(const void* q, const int64_t* q_strides, const void* k
                           int32_t page_size, int32_t dtype, float scale, int32_t max_kv_len,
                           int32_t* error_word, void* stream) {
   g_last_error.clear();
-  (void)q; (void)q_strides; (void)k_pool; (void)v_pool; (void)num_layers; (void)layer;
-  (void)capacity_tokens; (void)page_table; (void)page_table_stride; (void)cache_lens;
-  (void)out; (void)out_strides; (void)batch; (void)query_len; (void)num_q_heads;
-  (void)num_kv_heads; (void)head_dim; (void)page_size; (void)dtype; (void)scale;
-  (void)max_kv_len; (void)error_word; (void)stream;
-  return fail(HYT_ERR_UNSUPPORTED, "prefill kernel not built yet");
+  (void)max_kv_len;  // the prefill grid is sized by query_len, not by the longest request
+  int rc = check_attention_pointers(q, q_strides, k_pool, v_pool, page_table, cache_lens, out,
+                                    out_strides);
+  if (rc != HYT_OK) return rc;
+  Geometry g{num_layers, layer, capacity_tokens, page_table_stride, batch, query_len,
+             num_q_heads, num_kv_heads, head_dim, page_size, dtype};
+  rc = check_geometry(g);
+  if (rc != HYT_OK) return rc;
+  if (!prefill_eligible(g, q, q_strides, out, out_strides))
+    return fail(HYT_ERR_UNSUPPORTED,
+                "prefill kernel needs bf16/f16, head_dim 128, page_size % 128 == 0 and "
+                "16-byte aligned q/out rows");
+  return launch_prefill(q, q_strides, k_pool, v_pool, g, page_table, cache_lens, out,
+                        out_strides, scale, error_word, static_cast<cudaStream_t>(stream));
 }
 
 int hyt_paged_attention(const void* q, const int64_t* q_strides, const void* k_pool,
@@ -416,6 +455,9 @@ int hyt_paged_attention(const void* q, const int64_t* q_strides, const void* k_p
     return launch_decode(q, q_strides, k_pool, v_pool, g, page_table, cache_lens, out,
                          out_strides, scale, max_kv_len, split_tokens, workspace,
                          workspace_bytes, error_word, s);
+  if (prefill_eligible(g, q, q_strides, out, out_strides))
+    return launch_prefill(q, q_strides, k_pool, v_pool, g, page_table, cache_lens, out,
+                          out_strides, scale, error_word, s);
   return launch_generic(q, q_strides, k_pool, v_pool, g, page_table, cache_lens, out,
                         out_strides, scale, error_word, s);
 }

@@ -2,8 +2,8 @@
 //
 // Thin wrappers over documented PTX: mbarriers, TMA tensor loads, ldmatrix,
 // mma.sync, tcgen05 and the hardware ex2 instruction. Every wait on an
-// mbarrier is bounded: after kSpinLimit polls it records
-// HYT_DEVERR_WAIT_TIMEOUT and returns, so a logic error cannot hang the GPU.
+// mbarrier is bounded in time: it records HYT_DEVERR_WAIT_TIMEOUT and returns,
+// so a logic error cannot hang the GPU.
 #pragma once
 
 #include <cuda.h>
@@ -16,7 +16,7 @@
 
 namespace hyt {
 
-constexpr long long kSpinLimit = 1ll << 26;  // polls before a wait gives up (seconds, not hours)
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // one pipeline wait gives up after 1 s
 
 __device__ __forceinline__ void flag_error(int32_t* error_word, int bits) {
   if (error_word != nullptr) atomicOr(error_word, bits);
@@ -57,13 +57,40 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* error_word) {
-  for (long long i = 0; i < kSpinLimit; ++i) {
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait for the phase with the given parity to complete. `abort` is a
+// CTA-shared flag: once any wait of the CTA has given up, later waits return at
+// once, so a logic error costs about one second, never a hang.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* error_word,
+                                          volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  if (abort != nullptr && *abort) return false;
+  const uint64_t start = global_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 0) {
+      if (abort != nullptr && *abort) return false;
+      if (global_ns() - start > kWaitLimitNs) {
+        if (abort != nullptr) *abort = 1;
+        flag_error(error_word, HYT_DEVERR_WAIT_TIMEOUT);
+        return false;
+      }
+    }
   }
-  flag_error(error_word, HYT_DEVERR_WAIT_TIMEOUT);
-  return false;
+}
+
+// Wait (bounded by time only) for asynchronous work this CTA started, e.g. the
+// last TMA loads or tensor-core ops, so none is in flight when the CTA exits.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  const uint64_t start = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_ns() - start > kWaitLimitNs) return;
+  }
 }
 
 // ---------------------------------------------------------------- TMA
@@ -117,6 +144,102 @@ __device__ __forceinline__ void mma_16816(float* c, const uint32_t* a, uint32_t 
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
   }
+}
+
+// ---------------------------------------------------------------- tcgen05 / TMEM
+// Shared-memory matrix descriptor for a 128B-swizzled operand tile.
+// K-major: rows of 128 bytes, 8-row groups 1024 bytes apart (SBO), LBO unused (1).
+// MN-major: 64-element rows of 128 bytes along MN, next 64 MN elements `lbo_bytes`
+// away, 8-row groups along K 1024 bytes apart.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr, uint32_t lbo_bytes) {
+  uint64_t desc = 0;
+  desc |= uint64_t((smem_addr >> 4) & 0x3FFFu);
+  desc |= uint64_t((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  desc |= uint64_t(1024u >> 4) << 32;  // SBO: 8 rows x 128 B
+  desc |= uint64_t(1) << 46;           // descriptor version for sm_100
+  desc |= uint64_t(2) << 61;           // SWIZZLE_128B
+  return desc;
+}
+
+// Instruction descriptor of tcgen05.mma kind::f16 with an f32 accumulator.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(bool bf16, int m, int n, bool a_mn_major,
+                                                      bool b_mn_major) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
+         ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(smem_dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
+__device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on an mbarrier once every tcgen05 op this thread issued so far has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// 32 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Named barrier over a subset of the CTA's warps.
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 // ---------------------------------------------------------------- numerics

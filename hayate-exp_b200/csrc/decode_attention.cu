@@ -78,6 +78,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRingBytes);
   uint64_t* empty = full + kStages;
   int* s_last = reinterpret_cast<int*>(empty + kStages);
+  volatile int* s_abort = s_last + 1;  // set once a bounded wait gave up
 
   // ---- refuse page ids / lengths that would address outside the pool
   int bad = 0;
@@ -92,11 +93,14 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (page < 0 || page >= p.num_pages) bad |= HYT_DEVERR_PAGE_RANGE;
     }
   }
+  if (p.error_word != nullptr && (*reinterpret_cast<volatile int32_t*>(p.error_word) & HYT_DEVERR_WAIT_TIMEOUT))
+    bad |= HYT_DEVERR_WAIT_TIMEOUT;  // an earlier CTA's wait gave up: start no pipeline
   bad = __syncthreads_or(bad);
   if (bad && threadIdx.x == 0) flag_error(p.error_word, bad);
   if (nsplits > P.d.max_splits) nsplits = P.d.max_splits;
 
   if (threadIdx.x == 0) {
+    *s_abort = 0;
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
@@ -120,7 +124,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       tma_prefetch_desc(&v_map);
       for (int i = 0; i < n_tiles; ++i) {
         const int stage = i % kStages;
-        if (i >= kStages) mbar_wait(&empty[stage], ((i / kStages) - 1) & 1, p.error_word);
+        if (i >= kStages) mbar_wait(&empty[stage], ((i / kStages) - 1) & 1, p.error_word, s_abort);
         const int tok = tok_begin + i * kTile;
         const int32_t page = table[tok >> p.page_shift];
         const int row = (page << p.page_shift) + (tok & page_mask);
@@ -131,6 +135,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         tma_load_3d(dst + 2 * kBoxBytes, &v_map, &full[stage], 0, row, plane);
         tma_load_3d(dst + 3 * kBoxBytes, &v_map, &full[stage], 64, row, plane);
       }
+      // no TMA write may still be in flight when the ring is reused or the CTA exits
+      for (int i = max(0, n_tiles - kStages); i < n_tiles; ++i)
+        mbar_drain(&full[i % kStages], (i / kStages) & 1);
     }
   } else {
     // ------------------------------------------------------------ consumers
@@ -177,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
     for (int i = 0; i < n_tiles; ++i) {
       const int stage = i % kStages;
-      mbar_wait(&full[stage], (i / kStages) & 1, p.error_word);
+      mbar_wait(&full[stage], (i / kStages) & 1, p.error_word, s_abort);
       const uint32_t kbase = ring + stage * kStageBytes;
       const uint32_t vbase = kbase + 2 * kBoxBytes;
       const int key0 = warp * 16;  // this warp's keys inside the tile

@@ -58,4 +58,9 @@ cudaError_t run_decode_attention(const AttentionParams& p, const DecodeLaunch& d
                                  const CUtensorMap& k_map, const CUtensorMap& v_map, int dtype,
                                  cudaStream_t stream);
 
+// ------------------------------------------------------------ (b) tcgen05 chunked prefill
+// bf16/f16, head_dim 128, page_size % 128 == 0, q/out rows 16-byte aligned.
+cudaError_t run_prefill_attention(const AttentionParams& p, const CUtensorMap& k_map,
+                                  const CUtensorMap& v_map, int dtype, cudaStream_t stream);
+
 }  // namespace hyt

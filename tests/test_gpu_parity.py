@@ -182,3 +182,83 @@ def test_attend_output_layout_is_transpose_friendly():
     out = batch.attend_layer(q, 0)
     assert out.shape == q.shape
     assert out.transpose(1, 2).is_contiguous()
+
+
+PREFILL_CASES = [
+    ([0], 1), ([0, 5], 5), ([127, 128, 129], 128), ([0, 200, 1000], 130),
+    ([4095, 33], 512), ([1, 2048], 257), ([300], 1000),
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=str)
+@pytest.mark.parametrize("lengths, query_len", PREFILL_CASES, ids=str)
+def test_prefill_kernel_matches_oracle(lengths, query_len, dtype):
+    manager, _, batch, q, k, v = build_step(lengths, query_len, dtype=dtype, seed=len(lengths) + query_len)
+    manager.kernel = "prefill"
+    batch.write_layer(0, k, v)
+    out = batch.attend_layer(q, 0)
+    torch.cuda.synchronize()
+    manager.check_device_errors()
+    ref = oracle_out(manager, batch, q)
+    err = np.abs(out.float().cpu().numpy() - ref).max()
+    assert err <= 2e-2, err
+
+
+@pytest.mark.parametrize("page_size", [256, 512])
+def test_prefill_kernel_large_pages(page_size):
+    manager, _, batch, q, k, v = build_step([70, 600], 300, page_size=page_size, seed=page_size)
+    manager.kernel = "prefill"
+    batch.write_layer(0, k, v)
+    out = batch.attend_layer(q, 0)
+    torch.cuda.synchronize()
+    manager.check_device_errors()
+    err = np.abs(out.float().cpu().numpy() - oracle_out(manager, batch, q)).max()
+    assert err <= 2e-2, err
+
+
+def test_prefill_contiguous_q_and_multi_layer():
+    gen = torch.Generator(device="cuda").manual_seed(4)
+    manager = PagedKVCacheManager(3, 8, 128, 64 * 128, 128, 2, torch.bfloat16, "cuda")
+    W.shuffle_free_pages(manager, 4)
+    handles = [manager.allocate() for _ in range(2)]
+    for h, n in zip(handles, (100, 900)):
+        W.fill_history(manager, h, n, gen)
+    q, k, v = W.step_inputs(manager, handles, 64, 32, gen, strided=False)
+    batch = manager.begin_batch(handles, 64)
+    for layer in range(3):
+        batch.write_layer(layer, k, v)
+    out = batch.attend_layer(q, 2)
+    torch.cuda.synchronize()
+    manager.check_device_errors()
+    err = np.abs(out.float().cpu().numpy() - oracle_out(manager, batch, q, layer=2)).max()
+    assert err <= 2e-2, err
+
+
+def test_full_size_prefill_config():
+    """Config 3 shapes (8 requests x 512-token chunk on prefixes U[0, 4096])."""
+    rng = np.random.RandomState(1)
+    prefixes = [int(n) for n in rng.randint(0, 4097, size=8)]
+    manager, _, batch, q, k, v = build_step(prefixes, 512, seed=21)
+    batch.write_layer(0, k, v)
+    out = batch.attend_layer(q, 0)  # auto: the tcgen05 prefill kernel
+    manager.kernel = "generic"
+    ref_gpu = batch.attend_layer(q, 0)
+    torch.cuda.synchronize()
+    manager.check_device_errors()
+    assert (out.float() - ref_gpu.float()).abs().max().item() <= 2e-2
+    sample = [0, 5]
+    ref = oracle_out(manager, batch, q, requests=sample)
+    err = np.abs(out.float().cpu().numpy()[sample] - ref[sample]).max()
+    assert err <= 2e-2, err
+
+
+def test_prefill_flags_bad_page_ids():
+    manager, _, batch, q, k, v = build_step([300], 40, seed=2)
+    table = batch.page_table.clone()
+    table[0, 1] = -7
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = ops.paged_attention(q, manager.k_cache, manager.v_cache, 0, table, batch.cache_lens_i32,
+                              manager.page_size, 340, error_word=err, kernel="prefill")
+    torch.cuda.synchronize()
+    assert int(err.item()) & 1
+    assert float(out.float().abs().max()) == 0.0  # refused CTAs write zeros
