@@ -9,6 +9,11 @@
 #include "common.cuh"
 #include "kernels.cuh"
 
+// Split partials + arrival counters of hyt_decode_attention_noalloc, one copy per
+// GPU that loads this library. In host code this name is only a stand-in for the
+// symbol: its device address is looked up per device (decode_scratch_address).
+static __device__ __align__(256) uint8_t g_decode_scratch[HYT_NOALLOC_SCRATCH_BYTES];
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -313,6 +318,28 @@ int launch_generic(const void* q, const int64_t* qs, const void* k_pool, const v
   return HYT_OK;
 }
 
+// ------------------------------------------------------------------ static decode scratch
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+// Device address of g_decode_scratch on the current device (looked up once per device).
+int decode_scratch_address(void** out) {
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
+  if (device < 0 || device >= kMaxDevices) return fail(HYT_ERR_UNSUPPORTED, "device index too large");
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[device] == nullptr) {
+    void* addr = nullptr;
+    err = cudaGetSymbolAddress(&addr, g_decode_scratch);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaGetSymbolAddress(decode scratch)");
+    g_scratch_addr[device] = addr;
+  }
+  *out = g_scratch_addr[device];
+  return HYT_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -406,6 +433,50 @@ int hyt_decode_attention(const void* q, const int64_t* q_strides, const void* k_
   return launch_decode(q, q_strides, k_pool, v_pool, g, page_table, cache_lens, out,
                        out_strides, scale, max_kv_len, split_tokens, workspace, workspace_bytes,
                        error_word, static_cast<cudaStream_t>(stream));
+}
+
+int hyt_decode_attention_noalloc(const void* q, const int64_t* q_strides, const void* k_pool,
+                                 const void* v_pool, int32_t num_layers, int32_t layer,
+                                 int64_t capacity_tokens, const int32_t* page_table,
+                                 int32_t page_table_stride, const int32_t* cache_lens, void* out,
+                                 const int64_t* out_strides, int32_t batch, int32_t query_len,
+                                 int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                 int32_t page_size, int32_t dtype, float scale,
+                                 int32_t max_kv_len, int32_t split_tokens, int32_t* error_word,
+                                 void* stream) {
+  g_last_error.clear();
+  int rc = check_attention_pointers(q, q_strides, k_pool, v_pool, page_table, cache_lens, out,
+                                    out_strides);
+  if (rc != HYT_OK) return rc;
+  Geometry g{num_layers, layer, capacity_tokens, page_table_stride, batch, query_len,
+             num_q_heads, num_kv_heads, head_dim, page_size, dtype};
+  rc = check_geometry(g);
+  if (rc != HYT_OK) return rc;
+  if (!decode_eligible(g))
+    return fail(HYT_ERR_UNSUPPORTED,
+                "decode kernel needs bf16/f16, head_dim 128, page_size % 64 == 0 and "
+                "group * query_len <= 16");
+  if (max_kv_len < query_len) return fail(HYT_ERR_INVALID, "max_kv_len must be >= query_len");
+  if (split_tokens < 0) return fail(HYT_ERR_INVALID, "split_tokens must be >= 0");
+  const DecodeLayout L = decode_layout(batch, query_len, num_q_heads, num_kv_heads, max_kv_len,
+                                       split_tokens);
+  if (L.total > size_t(HYT_NOALLOC_SCRATCH_BYTES))
+    return fail(HYT_ERR_WORKSPACE,
+                "decode scratch of " + std::to_string(L.total) + " bytes exceeds the static " +
+                    std::to_string(HYT_NOALLOC_SCRATCH_BYTES) +
+                    "-byte buffer; pass a larger split_tokens or use hyt_decode_attention");
+  void* scratch = nullptr;
+  rc = decode_scratch_address(&scratch);
+  if (rc != HYT_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (L.total > 0) {
+    // the array keeps the previous call's bytes: the counters must start at zero
+    cudaError_t err = cudaMemsetAsync(scratch, 0, L.counter_bytes, s);
+    if (err != cudaSuccess) return cuda_fail(err, "clearing the decode scratch counters");
+  }
+  return launch_decode(q, q_strides, k_pool, v_pool, g, page_table, cache_lens, out, out_strides,
+                       scale, max_kv_len, split_tokens, scratch, HYT_NOALLOC_SCRATCH_BYTES,
+                       error_word, s);
 }
 
 int hyt_prefill_attention(const void* q, const int64_t* q_strides, const void* k_pool,

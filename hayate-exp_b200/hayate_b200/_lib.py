@@ -35,6 +35,7 @@ SIGNATURES = {
                                       _c_p, _c_p]),
     "hyt_paged_attention": (ctypes.c_int, _ATTENTION_ARGS + [_c_i32, _c_i32, _c_p, _c_size, _c_p, _c_p]),
     "hyt_decode_attention": (ctypes.c_int, _ATTENTION_ARGS + [_c_i32, _c_i32, _c_p, _c_size, _c_p, _c_p]),
+    "hyt_decode_attention_noalloc": (ctypes.c_int, _ATTENTION_ARGS + [_c_i32, _c_i32, _c_p, _c_p]),
     "hyt_prefill_attention": (ctypes.c_int, _ATTENTION_ARGS + [_c_i32, _c_p, _c_p]),
     "hyt_generic_attention": (ctypes.c_int, _ATTENTION_ARGS + [_c_p, _c_p]),
     "hyt_attention_workspace_bytes": (_c_size, [_c_i32] * 8),

@@ -109,6 +109,34 @@ int hyt_decode_attention(const void* q, const int64_t* q_strides, const void* k_
                          int32_t split_tokens, void* workspace, size_t workspace_bytes,
                          int32_t* error_word, void* stream);
 
+/*
+ * Split-KV decode that allocates nothing. No counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory: a C or FFI host that only
+ * borrows tensors from another framework's caching allocator and has no
+ * allocator of its own, or a serving loop that must not call cudaMalloc
+ * (which can synchronise the whole device) once it is running. Same arguments
+ * and results as hyt_decode_attention, minus the workspace: the split partials
+ * and arrival counters live in one static device array of
+ * HYT_NOALLOC_SCRATCH_BYTES that every GPU loading this library holds until
+ * the process exits. Sizes whose workspace (hyt_attention_workspace_bytes)
+ * exceeds it are refused with HYT_ERR_WORKSPACE; a larger split_tokens needs
+ * less. The first call on a device looks the array's address up (once per
+ * device), so make that first call before any stream capture. Every call
+ * clears the counter area on `stream` and then reuses the array, so calls
+ * that overlap on the GPU (other streams, other threads) race on it.
+ */
+#define HYT_NOALLOC_SCRATCH_BYTES (8u << 20)
+int hyt_decode_attention_noalloc(const void* q, const int64_t* q_strides, const void* k_pool,
+                                 const void* v_pool, int32_t num_layers, int32_t layer,
+                                 int64_t capacity_tokens, const int32_t* page_table,
+                                 int32_t page_table_stride, const int32_t* cache_lens, void* out,
+                                 const int64_t* out_strides, int32_t batch, int32_t query_len,
+                                 int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                 int32_t page_size, int32_t dtype, float scale,
+                                 int32_t max_kv_len, int32_t split_tokens, int32_t* error_word,
+                                 void* stream);
+
 /* tcgen05/TMEM chunked-prefill kernel only (bf16/f16, head_dim 128). */
 int hyt_prefill_attention(const void* q, const int64_t* q_strides, const void* k_pool,
                           const void* v_pool, int32_t num_layers, int32_t layer,
