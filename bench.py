@@ -443,6 +443,98 @@ def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=N
     }
 
 
+# ---------------------------------------------------------------------------- long decode (cfg 5)
+LONG_GROUPS, LONG_PER_GROUP, LONG_PREFIX, LONG_CONTEXT = 32, 16, 4096, 32768
+
+
+def run_longdecode(args, world, rank, local, peaks, peak_kind):
+    """512 requests x 32768-token context, groups of 16 alias a 4096-token prefix (shared
+    pages); every request decodes one token per step. Groups are split across ranks."""
+    import torch
+
+    from hayate_b200 import PagedKVCacheManager
+    from hayate_b200 import workloads as W
+
+    steps = args.steps
+    groups = [g for g in range(LONG_GROUPS) if g % world == rank]
+    n_req = len(groups) * LONG_PER_GROUP
+    own = LONG_CONTEXT - LONG_PREFIX
+    unique = len(groups) * (LONG_PREFIX + LONG_PER_GROUP * own)
+    pages = unique // 128 + n_req * (steps // 128 + 1) + 8
+    manager = PagedKVCacheManager(1, 8, 128, pages * 128, 128, n_req + len(groups),
+                                  torch.bfloat16, "cuda")
+    W.shuffle_free_pages(manager, 5000 + rank)
+    gen = torch.Generator(device="cuda").manual_seed(5000 + rank)
+    handles = []
+    for _ in groups:
+        root = manager.allocate()
+        W.fill_history(manager, root, LONG_PREFIX, gen)
+        for _ in range(LONG_PER_GROUP):
+            h = manager.share(root, LONG_PREFIX)              # prefix pages aliased, not copied
+            W.fill_history(manager, h, LONG_CONTEXT, gen, start=LONG_PREFIX)
+            handles.append(h)
+        manager.release(root)                                 # the 16 sharers keep the pages
+    inputs = [W.step_inputs(manager, handles, 1, 32, gen, lengths=[LONG_CONTEXT + s] * n_req)
+              for s in range(steps + args.warmup)]
+    torch.cuda.synchronize()
+
+    def step(s, ev=None):
+        batch = manager.begin_batch(handles, 1)
+        q, k, v = inputs[s]
+        batch.write_layer(0, k, v)
+        if ev is not None:
+            ev[0].record()
+        batch.attend_layer(q, 0)
+        if ev is not None:
+            ev[1].record()
+        manager.commit_batch(handles, 1)
+
+    for s in range(args.warmup):
+        step(steps + s)
+    torch.cuda.synchronize()
+    for h in handles:  # undo the warm-up appends so the timed steps start at 32768
+        manager.truncate(h, LONG_CONTEXT)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record()
+        for s in range(steps):
+            step(s, evs[s])
+        end.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    manager.check_device_errors()
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    attn_ms = sum(a.elapsed_time(b) for a, b in evs) / steps
+    row = 8 * 128 * 2 * 2  # K + V bytes per token
+    unique_per_step = sum(len(groups) * (LONG_PREFIX + LONG_PER_GROUP * (own + s + 1)) for s in range(steps)) * row / steps
+    logical_per_step = sum(n_req * (LONG_CONTEXT + s + 1) for s in range(steps)) * row / steps
+    achieved = unique_per_step / (attn_ms / 1e3) / 1e9
+    tokens = sum_over_ranks(float(n_req * steps), world)
+    return {
+        "metric": "long-context decode tok/s (config 5)", "value": round(tokens / (ms / 1e3), 1),
+        "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / steps, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1), QK-norm + RoPE theta 1e6, shuffled pages",
+        "config": {"workload": "config 5: 512 requests x 32768 context, groups of 16 share a 4096-token prefix, 1 layer",
+                   "requests_this_rank": n_req, "groups_this_rank": len(groups),
+                   "parallelism": f"request-parallel by prefix group x{world}",
+                   "l2": "KV read per step tens of GB >> 126 MB L2"},
+        "unique_GB_per_step_this_rank": round(unique_per_step / 1e9, 2),
+        "logical_GB_per_step_this_rank": round(logical_per_step / 1e9, 2),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "bytes": "unique (shared prefix pages once)",
+                     "logical_GB_s": round(logical_per_step / (attn_ms / 1e3) / 1e9, 1), "traffic": None,
+                     "kernel": "decode_attention_kernel"},
+        "attention_ms_per_step": round(attn_ms, 4),
+        "gpu_launches": 2 * steps,
+        "clocks": clocks.summary(),
+    }
+
+
 # ---------------------------------------------------------------------------- reference arm
 def run_reference(args, world, rank):
     """CPU oracle on the host cores, same metric/unit/config as the GPU arm (rank 0 only)."""
@@ -516,7 +608,7 @@ def main():
     elif args.workload == "prefill":
         result = run_prefill(args, world, rank, local, peaks, peak_kind)
     else:
-        raise SystemExit(f"workload {args.workload} is not built yet")
+        result = run_longdecode(args, world, rank, local, peaks, peak_kind)
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:

@@ -57,36 +57,40 @@ def shuffle_free_pages(manager: PagedKVCacheManager, seed: int) -> None:
 
 
 def fill_history(manager: PagedKVCacheManager, handle: PagedCacheHandle, length: int,
-                 gen: torch.Generator, layers=None, chunk: int = 8192) -> None:
-    """Give ``handle`` ``length`` tokens of synthetic K/V (written straight into its pages)."""
+                 gen: torch.Generator, layers=None, chunk: int = 8192, start: int = 0) -> None:
+    """Give ``handle`` tokens ``start .. length - 1`` of synthetic K/V (written into its pages).
+
+    With ``start > 0`` the first ``start`` tokens are kept (e.g. a shared prefix).
+    """
     manager.reserve(handle, length)
     device, dtype = manager.k_cache.device, manager.k_cache.dtype
     H, D, P = manager.num_kv_heads, manager.head_dim, manager.page_size
     layers = range(manager.num_layers) if layers is None else layers
     pages = torch.tensor(handle.pages, dtype=torch.int64, device=device)
-    for start in range(0, length, chunk):
-        stop = min(length, start + chunk)
-        pos = torch.arange(start, stop, device=device)
+    for first in range(start, length, chunk):
+        stop = min(length, first + chunk)
+        pos = torch.arange(first, stop, device=device)
         slots = pages[pos // P] * P + pos % P
         for layer in layers:
-            k = qk_tokens((H, stop - start, D), pos, dtype, device, gen)
-            v = v_tokens((H, stop - start, D), dtype, device, gen)
+            k = qk_tokens((H, stop - first, D), pos, dtype, device, gen)
+            v = v_tokens((H, stop - first, D), dtype, device, gen)
             manager.k_cache[layer, 0].index_copy_(1, slots, k)
             manager.v_cache[layer, 0].index_copy_(1, slots, v)
     handle.length = length
 
 
 def step_inputs(manager: PagedKVCacheManager, handles, query_len: int, num_q_heads: int,
-                gen: torch.Generator, strided: bool = True):
+                gen: torch.Generator, strided: bool = True, lengths=None):
     """q ``[B, H_q, T, D]`` and new k/v ``[B, H_kv, T, D]`` for one step at true positions.
 
     With ``strided`` the tensors are ``[B, T, H, D]`` memory viewed as
-    ``[B, H, T, D]``, the layout hayate's attention module hands over.
+    ``[B, H, T, D]``, the layout hayate's attention module hands over. ``lengths``
+    overrides the handles' current lengths (inputs for a later step).
     """
     device, dtype = manager.k_cache.device, manager.k_cache.dtype
     H, D = manager.num_kv_heads, manager.head_dim
     B = len(handles)
-    lens = torch.tensor([h.length for h in handles], device=device)
+    lens = torch.tensor([h.length for h in handles] if lengths is None else list(lengths), device=device)
     pos = lens[:, None] + torch.arange(query_len, device=device)[None, :]  # [B, T]
 
     def make(heads, is_qk):
