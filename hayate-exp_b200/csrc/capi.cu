@@ -283,8 +283,10 @@ bool rows_16b_aligned(const void* ptr, const int64_t* strides) {
 
 bool prefill_eligible(const Geometry& g, const void* q, const int64_t* qs, const void* out,
                       const int64_t* os) {
+  // the kernel pairs two query heads of one KV group per CTA
   return (g.dtype == HYT_DTYPE_BF16 || g.dtype == HYT_DTYPE_F16) && g.head_dim == 128 &&
-         g.page_size % 128 == 0 && rows_16b_aligned(q, qs) && rows_16b_aligned(out, os);
+         g.page_size % 128 == 0 && (g.num_q_heads / g.num_kv_heads) % 2 == 0 &&
+         rows_16b_aligned(q, qs) && rows_16b_aligned(out, os);
 }
 
 int launch_prefill(const void* q, const int64_t* qs, const void* k_pool, const void* v_pool,
@@ -498,8 +500,8 @@ int hyt_prefill_attention(const void* q, const int64_t* q_strides, const void* k
   if (rc != HYT_OK) return rc;
   if (!prefill_eligible(g, q, q_strides, out, out_strides))
     return fail(HYT_ERR_UNSUPPORTED,
-                "prefill kernel needs bf16/f16, head_dim 128, page_size % 128 == 0 and "
-                "16-byte aligned q/out rows");
+                "prefill kernel needs bf16/f16, head_dim 128, page_size % 128 == 0, an even "
+                "query-head group and 16-byte aligned q/out rows");
   return launch_prefill(q, q_strides, k_pool, v_pool, g, page_table, cache_lens, out,
                         out_strides, scale, error_word, static_cast<cudaStream_t>(stream));
 }

@@ -200,6 +200,18 @@ __device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, ui
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T: A (M x K, 16-bit, two elements per 32-bit column,
+// row m in lane m) read from tensor memory.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on an mbarrier once every tcgen05 op this thread issued so far has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -228,6 +240,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
       "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
       "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+// 16 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
       : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() {
@@ -277,5 +299,22 @@ struct Elem<float> {
 };
 
 constexpr float kLog2e = 1.4426950408889634f;
+
+// 2^x on the FMA pipe, for x <= 64 (x below -126, -inf included, gives 0).
+// Cody-Waite split x = i + f, i = floor(x) taken from the mantissa of x + 1.5 * 2^23
+// rounded down, f in [0, 1); 2^f from a cubic fitted here to 2^f on [0, 1) in relative
+// error (iteratively reweighted least squares; max relative error 7.5e-5, far below the
+// 2^-9 of the bf16/f16 P it feeds); the exponent field then gets i added.
+__device__ __forceinline__ float ex2_poly(float x) {
+  const float xc = fmaxf(x, -126.f);
+  const float shifted = __fadd_rd(xc, 12582912.f);  // 1.5 * 2^23
+  const float fl = shifted - 12582912.f;
+  const float f = xc - fl;
+  float p = fmaf(0.0780240297f, f, 0.226067066f);
+  p = fmaf(p, f, 0.695834041f);
+  p = fmaf(p, f, 0.999925137f);
+  const float r = __int_as_float(__float_as_int(p) + (__float_as_int(shifted) << 23));
+  return x < -126.f ? 0.f : r;  // masked scores (-inf) give exactly 0, like ex2
+}
 
 }  // namespace hyt

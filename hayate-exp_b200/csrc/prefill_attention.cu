@@ -5,25 +5,29 @@
 // of request b sees logical keys 0 .. cache_lens[b] + t (paged_cache.py:266-271),
 // query head h reads KV head h / (H_q / H_kv), scale 1/sqrt(128) by default.
 //
-// Work unit: one CTA per (128 consecutive queries of one query head, request).
-// 192 threads, warp-specialised:
-//   warps 0-3 (softmax warpgroup): thread r owns query row r. It loads its Q row
-//     into 128B-swizzled shared memory, then for every 128-key tile reads its S
-//     row from TMEM (tcgen05.ld), applies the causal mask, runs a base-2 online
-//     softmax (the running max is only moved when it grows by more than 2^8, so
-//     O is rescaled rarely; the final O / l is exact either way), writes its P row
-//     as bf16/f16 into swizzled shared memory and, when the max moved, rescales
-//     its O row in TMEM. At the end it normalises O and stores the output row.
-//   warp 4 (producer): per 128-key tile looks the page up in the page table and
-//     TMA-loads the K and V tiles (2 boxes of [128 tokens x 64 dims] each, 128B
-//     swizzle) into 2-stage rings.
-//   warp 5 (MMA issuer, one thread): S = Q K^T into one of two TMEM S buffers
-//     (M=128, N=128, 8 x K=16), then O += P V (V as an MN-major operand), each
-//     batch closed by tcgen05.commit onto the mbarriers the other warps wait on.
-//     QK of tile j+1 is issued before PV of tile j so the tensor core works on
-//     it while the softmax warps handle tile j.
-// TMEM: S0 cols [0,128), S1 [128,256), O [256,384) of a 512-column allocation.
-// Shared memory: Q 32 KB, K 2x32 KB, V 2x32 KB, P 2x32 KB (about 225 KB).
+// Work unit: one CTA per (128 consecutive query positions, pair of query heads of
+// one KV group, request). The two heads are two 128-row tiles, A and B, that see the
+// same keys under the same causal mask, so every K/V tile loaded serves both.
+// 320 threads, warp-specialised:
+//   warps 0-3 / 4-7 (softmax warpgroups A / B): thread r owns query row r of its
+//     tile (TMEM lane r). Per 128-key tile it reads its S row (tcgen05.ld), masks
+//     `key <= cache_len + t`, keeps a stale running max unless the true one grows
+//     by more than 2^8 (then rescales its O row in TMEM; O / l stays exact), turns
+//     the row into P with 3 of 4 exponentials on MUFU (ex2) and 1 of 4 on the FMA
+//     pipe (ex2_poly), and writes P as packed bf16/f16 back over its S columns
+//     (tcgen05.st). At the end it normalises its O row and stores it.
+//   warp 8 (producer): per 128-key tile looks the page up and TMA-loads K and V
+//     (2 boxes of [128 tokens x 64 dims] each, 128B swizzle) into 2-stage rings.
+//   warp 9 (MMA issuer, one thread): S_x = Q_x K^T (M=128, N=128, 8 x K=16) and
+//     O_x += P_x V with P read straight from TMEM (tcgen05.mma, A in TMEM) and V as an
+//     MN-major shared-memory operand. Issue order per key tile j:
+//       PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1)
+//     so warpgroup A's softmax of tile j+1 overlaps the tensor core working on B
+//     and vice versa. tcgen05.mma ops of one thread execute in issue order, which
+//     is what lets QK_x(j+1) overwrite the columns PV_x(j) reads P from, and makes
+//     O_x stable whenever S_x(j) is (its commit covers PV_x(j-1)).
+// TMEM (512 columns): S_A/P_A [0,128), S_B/P_B [128,256), O_A [256,384), O_B [384,512).
+// Shared memory: Q_A, Q_B 32 KB each, K and V 2 x 32 KB each (192 KB).
 //
 // FLOPs per launch counted by the roofline: 4 * H_q * 128 per causal-valid
 // (query, key) pair.
@@ -36,17 +40,18 @@ namespace hyt {
 
 namespace {
 
-constexpr int kRows = 128;  // queries per CTA
-constexpr int kKeys = 128;  // keys per tile
+constexpr int kRows = 128;  // query positions per CTA (per tile)
+constexpr int kKeys = 128;  // keys per KV tile
 constexpr int kD = 128;
-constexpr int kThreads = 192;
-constexpr int kTileBytes = kRows * kD * 2;  // 32 KB
-constexpr int kChunkBytes = kTileBytes / 2; // [128 rows x 64 elements]
-constexpr int kQOff = 0;
-constexpr int kKOff = kQOff + kTileBytes;
+constexpr int kSoftmaxThreads = 256;
+constexpr int kProducerWarp = 8, kMmaWarp = 9;
+constexpr int kThreads = 320;
+constexpr int kTileBytes = kRows * kD * 2;   // 32 KB
+constexpr int kChunkBytes = kTileBytes / 2;  // [128 rows x 64 elements]
+constexpr int kQOff = 0;                     // Q_A, Q_B
+constexpr int kKOff = kQOff + 2 * kTileBytes;
 constexpr int kVOff = kKOff + 2 * kTileBytes;
-constexpr int kPOff = kVOff + 2 * kTileBytes;
-constexpr int kBarOff = kPOff + 2 * kTileBytes;
+constexpr int kBarOff = kVOff + 2 * kTileBytes;
 constexpr int kSmemBytes = kBarOff + 256 + 1024;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kOCol = 256;
@@ -66,8 +71,8 @@ __device__ __forceinline__ uint32_t sw128_offset(int r, int chunk) {
 struct Barriers {
   uint64_t q_full;
   uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
-  uint64_t s_full[2], s_free[2], p_full[2], p_empty[2];
-  uint64_t drain;
+  uint64_t s_full[2], p_full[2];  // per tile (A, B)
+  uint64_t o_done, drain;
   uint32_t tmem_base;
   int32_t abort;  // set once a bounded wait gave up: later waits return at once
 };
@@ -80,8 +85,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                              const PrefillKernelParams P) {
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   const AttentionParams& p = P.a;
-  const int q_tile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int g = h / P.group;
+  // heavier (later) query tiles first: they see the most keys
+  const int q_tile = int(gridDim.x) - 1 - int(blockIdx.x);
+  const int pair = blockIdx.y, b = blockIdx.z;
+  const int h0 = pair * 2;  // tiles A and B: heads h0 and h0 + 1 of KV group g
+  const int g = h0 / P.group;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   extern __shared__ uint8_t smem_raw[];
@@ -97,9 +105,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ---- refuse page ids that would address outside the pool (before any load)
   int bad = cache_len < 0 ? HYT_DEVERR_TABLE_RANGE : 0;
-  // a wait of an earlier CTA already gave up: do not start another pipeline
   if (p.error_word != nullptr && (*reinterpret_cast<volatile int32_t*>(p.error_word) & HYT_DEVERR_WAIT_TIMEOUT))
-    bad |= HYT_DEVERR_WAIT_TIMEOUT;
+    bad |= HYT_DEVERR_WAIT_TIMEOUT;  // an earlier CTA's wait gave up: start no pipeline
   for (int j = threadIdx.x; j < n_tiles && !bad; j += kThreads) {
     const int lp = (j * kKeys) >> p.page_shift;
     if (lp >= p.page_table_stride) {
@@ -112,11 +119,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   bad = __syncthreads_or(bad);
   if (bad) {
     if (threadIdx.x == 0) flag_error(p.error_word, bad);
-    // write zeros for this CTA's rows so the output is defined
-    for (int idx = threadIdx.x; idx < kRows * kD; idx += kThreads) {
-      const int r = idx / kD, d = idx - r * kD;
+    for (int idx = threadIdx.x; idx < 2 * kRows * kD; idx += kThreads) {
+      const int x = idx / (kRows * kD), r = (idx / kD) % kRows, d = idx % kD;
       if (t0 + r < p.query_len) {
-        T* out = static_cast<T*>(p.out) + b * p.o_sb + int64_t(h) * p.o_sh + int64_t(t0 + r) * p.o_st;
+        T* out = static_cast<T*>(p.out) + b * p.o_sb + int64_t(h0 + x) * p.o_sh + int64_t(t0 + r) * p.o_st;
         out[d] = Elem<T>::from_float(0.f);
       }
     }
@@ -125,18 +131,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     bars->abort = 0;
-    mbar_init(&bars->drain, 1);
-    mbar_init(&bars->q_full, 128);
+    mbar_init(&bars->q_full, kSoftmaxThreads);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->k_empty[s], 1);
       mbar_init(&bars->v_full[s], 1);
       mbar_init(&bars->v_empty[s], 1);
       mbar_init(&bars->s_full[s], 1);
-      mbar_init(&bars->s_free[s], 128);
-      mbar_init(&bars->p_full[s], 128);
-      mbar_init(&bars->p_empty[s], 1);
+      mbar_init(&bars->p_full[s], kRows);
     }
+    mbar_init(&bars->o_done, 1);
+    mbar_init(&bars->drain, 1);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -149,8 +154,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = bars->tmem_base;
   const uint32_t smem_base = smem_u32(smem);
   int32_t* err = p.error_word;
+  volatile int* abort = &bars->abort;
 
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&k_map);
@@ -162,83 +168,93 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int tok = j * kKeys;
         const int32_t page = table[tok >> p.page_shift];
         const int row = (page << p.page_shift) + (tok & page_mask);
-        if (j >= 2) mbar_wait(&bars->k_empty[st], ph ^ 1, err, &bars->abort);
+        if (j >= 2) mbar_wait(&bars->k_empty[st], ph ^ 1, err, abort);
         uint8_t* kdst = smem + kKOff + st * kTileBytes;
         mbar_arrive_expect_tx(&bars->k_full[st], kTileBytes);
         tma_load_3d(kdst, &k_map, &bars->k_full[st], 0, row, plane);
         tma_load_3d(kdst + kChunkBytes, &k_map, &bars->k_full[st], 64, row, plane);
-        if (j >= 2) mbar_wait(&bars->v_empty[st], ph ^ 1, err, &bars->abort);
+        if (j >= 2) mbar_wait(&bars->v_empty[st], ph ^ 1, err, abort);
         uint8_t* vdst = smem + kVOff + st * kTileBytes;
         mbar_arrive_expect_tx(&bars->v_full[st], kTileBytes);
         tma_load_3d(vdst, &v_map, &bars->v_full[st], 0, row, plane);
         tma_load_3d(vdst + kChunkBytes, &v_map, &bars->v_full[st], 64, row, plane);
       }
-      // no TMA write may still be in flight when the CTA exits
-      for (int j = max(0, n_tiles - 2); j < n_tiles; ++j) {
+      for (int j = max(0, n_tiles - 2); j < n_tiles; ++j) {  // nothing in flight at exit
         mbar_drain(&bars->k_full[j & 1], (j >> 1) & 1);
         mbar_drain(&bars->v_full[j & 1], (j >> 1) & 1);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_qk = umma_idesc_f16(kBf16, 128, 128, false, false);
       constexpr uint32_t idesc_pv = umma_idesc_f16(kBf16, 128, 128, false, true);
       auto kmajor = [&](uint32_t base, int kk) {
-        // k-step kk (16 elements): chunk kk/4, 32-byte step inside the 128B atom
         return umma_desc_sw128(base + (kk >> 2) * kChunkBytes + (kk & 3) * 32, 16);
       };
-      auto issue_pv = [&](int i) {
-        const int st = i & 1;
-        const uint32_t ph = (i >> 1) & 1;
-        mbar_wait(&bars->v_full[st], ph, err, &bars->abort);
-        mbar_wait(&bars->p_full[st], ph, err, &bars->abort);
-        tc_fence_after();
-        const uint32_t pbase = smem_base + kPOff + st * kTileBytes;
-        const uint32_t vbase = smem_base + kVOff + st * kTileBytes;
+      auto issue_qk = [&](int x, int j) {  // S_x = Q_x K_j^T
+        const uint32_t qbase = smem_base + kQOff + x * kTileBytes;
+        const uint32_t kbase = smem_base + kKOff + (j & 1) * kTileBytes;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          // V is [keys x dims]: K-dim = keys (16 per step = 2048 bytes), N = dims (LBO = chunk)
-          const uint64_t vdesc = umma_desc_sw128(vbase + kk * 2048, kChunkBytes);
-          umma_f16_ss(tmem + kOCol, kmajor(pbase, kk), vdesc, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(&bars->p_empty[st]);
-        umma_commit(&bars->v_empty[st]);
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16_ss(tmem + x * 128, kmajor(qbase, kk), kmajor(kbase, kk), idesc_qk, kk > 0 ? 1u : 0u);
+        umma_commit(&bars->s_full[x]);
       };
-      mbar_wait(&bars->q_full, 0, err, &bars->abort);
-      tc_fence_after();
-      const uint32_t qbase = smem_base + kQOff;
-      for (int j = 0; j < n_tiles; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        mbar_wait(&bars->k_full[st], ph, err, &bars->abort);
-        if (j >= 2) mbar_wait(&bars->s_free[st], ph ^ 1, err, &bars->abort);
-        tc_fence_after();
-        const uint32_t kbase = smem_base + kKOff + st * kTileBytes;
+      auto issue_pv = [&](int x, int j) {  // O_x += P_x V_j, P_x in TMEM over S_x
+        const uint32_t vbase = smem_base + kVOff + (j & 1) * kTileBytes;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          umma_f16_ss(tmem + st * 128, kmajor(qbase, kk), kmajor(kbase, kk), idesc_qk, kk > 0 ? 1u : 0u);
+          const uint64_t vdesc = umma_desc_sw128(vbase + kk * 2048, kChunkBytes);
+          umma_f16_ts(tmem + kOCol + x * 128, tmem + x * 128 + kk * 8, vdesc, idesc_pv,
+                      (j > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&bars->s_full[st]);
-        umma_commit(&bars->k_empty[st]);
-        if (j >= 1) issue_pv(j - 1);
+      };
+      mbar_wait(&bars->q_full, 0, err, abort);
+      mbar_wait(&bars->k_full[0], 0, err, abort);
+      tc_fence_after();
+      issue_qk(0, 0);
+      issue_qk(1, 0);
+      umma_commit(&bars->k_empty[0]);
+      for (int j = 0; j < n_tiles; ++j) {
+        const bool more = j + 1 < n_tiles;
+        mbar_wait(&bars->v_full[j & 1], (j >> 1) & 1, err, abort);
+        // tile A
+        mbar_wait(&bars->p_full[0], j & 1, err, abort);
+        tc_fence_after();
+        issue_pv(0, j);
+        if (more) {
+          mbar_wait(&bars->k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, err, abort);
+          tc_fence_after();
+          issue_qk(0, j + 1);
+        }
+        // tile B
+        mbar_wait(&bars->p_full[1], j & 1, err, abort);
+        tc_fence_after();
+        issue_pv(1, j);
+        umma_commit(&bars->v_empty[j & 1]);
+        if (more) {
+          issue_qk(1, j + 1);
+          umma_commit(&bars->k_empty[(j + 1) & 1]);
+        }
       }
-      issue_pv(n_tiles - 1);
+      umma_commit(&bars->o_done);
       umma_commit(&bars->drain);  // every MMA done before TMEM is released
       mbar_drain(&bars->drain, 0);
     }
   } else {
-    // ------------------------------------------------------------ softmax warpgroup
-    const int r = threadIdx.x;  // 0..127: query row == TMEM lane
+    // ------------------------------------------------------------ softmax warpgroups
+    const int x = warp >> 2;                   // tile: 0 = A, 1 = B
+    const int r = threadIdx.x - x * kRows;     // query row == TMEM lane
+    const int h = h0 + x;
     const int t = t0 + r;
     const bool row_valid = t < p.query_len;
     const int limit = cache_len + min(t, p.query_len - 1);  // last visible key
-    const uint32_t lane_addr = tmem + (uint32_t(warp * 32) << 16);
+    const uint32_t lane_addr = tmem + (uint32_t((warp & 3) * 32) << 16);
+    const uint32_t s_col = x * 128, o_col = kOCol + x * 128;
 
-    // Q row -> swizzled shared memory (zeros past the chunk)
-    {
+    {  // Q row -> swizzled shared memory (zeros past the chunk)
       const T* qrow = static_cast<const T*>(p.q) + b * p.q_sb + int64_t(h) * p.q_sh + int64_t(t) * p.q_st;
-      uint8_t* qdst = smem + kQOff;
+      uint8_t* qdst = smem + kQOff + x * kTileBytes;
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
@@ -252,96 +268,84 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float scale_log2 = p.scale * kLog2e;
     float m_run = -INFINITY, l_run = 0.f;
     for (int j = 0; j < n_tiles; ++j) {
-      const int st = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      mbar_wait(&bars->s_full[st], ph, err, &bars->abort);
+      mbar_wait(&bars->s_full[x], j & 1, err, abort);
       tc_fence_after();
       float s[128];
       {
-        uint32_t raw[32];
+        uint32_t raw[4][32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(lane_addr + st * 128 + c * 32, raw);
-          tmem_wait_ld();
+        for (int c = 0; c < 4; ++c) tmem_ld32(lane_addr + s_col + c * 32, raw[c]);
+        tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(raw[i]);
-        }
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(raw[c][i]);
       }
-      tc_fence_before();
-      mbar_arrive(&bars->s_free[st]);
-
-      // mask + tile max (scores in log2 units)
+      // mask + row max on the raw scores (scale > 0 keeps the order)
       const int key0 = j * kKeys;
-      float mx = -INFINITY;
-      if (key0 + kKeys - 1 <= limit) {
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+      if (key0 + kKeys - 1 > limit) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          s[c] *= scale_log2;
-          mx = fmaxf(mx, s[c]);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          s[c] = (key0 + c <= limit) ? s[c] * scale_log2 : -INFINITY;
-          mx = fmaxf(mx, s[c]);
-        }
+        for (int c = 0; c < 128; ++c)
+          if (key0 + c > limit) s[c] = -INFINITY;
       }
-      const float m_new = fmaxf(m_run, mx);
-      const bool warp_moves = __any_sync(0xffffffffu, m_new > m_run + kRescaleThreshold);
+#pragma unroll
+      for (int c = 0; c < 128; c += 2) {
+        mx0 = fmaxf(mx0, s[c]);
+        mx1 = fmaxf(mx1, s[c + 1]);
+      }
+      const float m_tile = fmaxf(mx0, mx1) * scale_log2;
+      const float m_new = fmaxf(m_run, m_tile);
+      const bool moves = __any_sync(0xffffffffu, m_new > m_run + kRescaleThreshold);
       float alpha = 1.f;
-      if (warp_moves) {
+      if (moves) {
         alpha = ex2(m_run - m_new);  // 0 on the first tile (m_run = -inf)
         m_run = m_new;
       }
-      float rowsum = 0.f;
-      uint32_t packed[64];
+      // P = 2^(s * scale_log2 - m) -> packed 16-bit pairs over the S columns
+      float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float p0 = ex2(s[2 * c] - m_run);
-        const float p1 = ex2(s[2 * c + 1] - m_run);
-        rowsum += p0 + p1;
-        packed[c] = Elem<T>::pack2(p0, p1);
-      }
-      l_run = l_run * alpha + rowsum;
-
-      // P row -> swizzled shared memory (buffer st is free once PV(j-2) completed)
-      if (j >= 2) mbar_wait(&bars->p_empty[st], ph ^ 1, err, &bars->abort);
-      uint8_t* pdst = smem + kPOff + st * kTileBytes;
+      for (int c = 0; c < 4; ++c) {
+        uint32_t packed[16];
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        *reinterpret_cast<uint4*>(pdst + sw128_offset(r, c)) =
-            make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+        for (int i = 0; i < 16; ++i) {
+          const int k = c * 32 + 2 * i;
+          const float a = fmaf(s[k], scale_log2, -m_run);
+          const float bb = fmaf(s[k + 1], scale_log2, -m_run);
+          const float pa = ex2(a);
+          const float pb = (i & 1) ? ex2_poly(bb) : ex2(bb);  // 1 in 4 on the FMA pipe
+          sum0 += pa;
+          sum1 += pb;
+          packed[i] = Elem<T>::pack2(pa, pb);
+        }
+        tmem_st16(lane_addr + s_col + c * 16, packed);
       }
-
-      // rescale O (the running max moved) once PV(j-1) has landed in TMEM
-      if (warp_moves && j >= 1) {
-        mbar_wait(&bars->p_empty[(j - 1) & 1], ((j - 1) >> 1) & 1, err, &bars->abort);
-        tc_fence_after();
+      l_run = l_run * alpha + (sum0 + sum1);
+      if (moves && j > 0) {  // O_x is stable: PV_x(j-1) completed before S_x(j) did
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
-          tmem_ld32(lane_addr + kOCol + c * 32, o);
+          tmem_ld32(lane_addr + o_col + c * 32, o);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(lane_addr + kOCol + c * 32, o);
+          tmem_st32(lane_addr + o_col + c * 32, o);
         }
-        tmem_wait_st();
       }
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bars->p_full[st]);
+      mbar_arrive(&bars->p_full[x]);
     }
 
     // ---- epilogue: O / l -> out[b, h, t, :]
-    mbar_wait(&bars->p_empty[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1, err, &bars->abort);
+    mbar_wait(&bars->o_done, 0, err, abort);
     tc_fence_after();
     const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
     T* out = static_cast<T*>(p.out) + b * p.o_sb + int64_t(h) * p.o_sh + int64_t(t) * p.o_st;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       uint32_t o[32];
-      tmem_ld32(lane_addr + kOCol + c * 32, o);
+      tmem_ld32(lane_addr + o_col + c * 32, o);
       tmem_wait_ld();
       if (row_valid) {
 #pragma unroll
@@ -373,7 +377,7 @@ cudaError_t run_prefill_attention(const AttentionParams& p, const CUtensorMap& k
   PrefillKernelParams P;
   P.a = p;
   P.group = p.num_q_heads / p.num_kv_heads;
-  const dim3 grid(unsigned((p.query_len + kRows - 1) / kRows), unsigned(p.num_q_heads),
+  const dim3 grid(unsigned((p.query_len + kRows - 1) / kRows), unsigned(p.num_q_heads / 2),
                   unsigned(p.batch));
   if (dtype == HYT_DTYPE_F16) {
     auto kernel = prefill_attention_kernel<__half>;

@@ -13,6 +13,7 @@ from .paged_cache import (
     PagedKVBatch,
     PagedKVCacheManager,
 )
+from .prefix_cache import PagedPrefixCache, PrefixCacheMatch
 from . import ops
 
 __all__ = [
@@ -21,5 +22,7 @@ __all__ = [
     "PagedCacheHandle",
     "PagedKVBatch",
     "PagedKVCacheManager",
+    "PagedPrefixCache",
+    "PrefixCacheMatch",
     "ops",
 ]
