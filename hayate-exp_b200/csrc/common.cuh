@@ -12,7 +12,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/hayate_b200.h"
+#include "hayate_b200.h"
 
 namespace hyt {
 
@@ -299,6 +299,32 @@ struct Elem<float> {
 };
 
 constexpr float kLog2e = 1.4426950408889634f;
+
+// ---------------------------------------------------------------- packed fp32 pairs
+// sm_100 executes fp32 add/mul/fma on two packed values per instruction.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 
 // 2^x on the FMA pipe, for x <= 64 (x below -126, -inf included, gives 0).
 // Cody-Waite split x = i + f, i = floor(x) taken from the mantissa of x + 1.5 * 2^23

@@ -13,9 +13,11 @@
 //     tile (TMEM lane r). Per 128-key tile it reads its S row (tcgen05.ld), masks
 //     `key <= cache_len + t`, keeps a stale running max unless the true one grows
 //     by more than 2^8 (then rescales its O row in TMEM; O / l stays exact), turns
-//     the row into P with 3 of 4 exponentials on MUFU (ex2) and 1 of 4 on the FMA
-//     pipe (ex2_poly), and writes P as packed bf16/f16 back over its S columns
-//     (tcgen05.st). At the end it normalises its O row and stores it.
+//     the row into P (scale-and-shift and row sums on packed f32x2 pairs, 7 of 8
+//     exponentials on MUFU and 1 of 8 on the FMA pipe via ex2_poly; masked keys
+//     give exact 0 on both), and writes P as packed bf16/f16
+//     back over its S columns (tcgen05.st). At the end it normalises its O row and
+//     stores it.
 //   warp 8 (producer): per 128-key tile looks the page up and TMA-loads K and V
 //     (2 boxes of [128 tokens x 64 dims] each, 128B swizzle) into 2-stage rings.
 //   warp 9 (MMA issuer, one thread): S_x = Q_x K^T (M=128, N=128, 8 x K=16) and
@@ -78,8 +80,9 @@ struct Barriers {
 };
 static_assert(sizeof(Barriers) <= 256, "barrier block");
 
+// 168 registers: 10 warps over 4 sub-partitions put 3 warps on one 16K-register file.
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __maxnreg__(168)
     prefill_attention_kernel(const __grid_constant__ CUtensorMap k_map,
                              const __grid_constant__ CUtensorMap v_map,
                              const PrefillKernelParams P) {
@@ -283,16 +286,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // mask + row max on the raw scores (scale > 0 keeps the order)
       const int key0 = j * kKeys;
-      float mx0 = -INFINITY, mx1 = -INFINITY;
-      if (key0 + kKeys - 1 > limit) {
+      const bool masked = key0 + kKeys - 1 > limit;  // only the diagonal tiles
+      if (masked) {
 #pragma unroll
         for (int c = 0; c < 128; ++c)
           if (key0 + c > limit) s[c] = -INFINITY;
       }
+      float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 128; c += 2) {
-        mx0 = fmaxf(mx0, s[c]);
-        mx1 = fmaxf(mx1, s[c + 1]);
+      for (int c = 0; c < 128; c += 4) {
+        mx0 = fmax3(mx0, s[c], s[c + 1]);
+        mx1 = fmax3(mx1, s[c + 2], s[c + 3]);
       }
       const float m_tile = fmaxf(mx0, mx1) * scale_log2;
       const float m_new = fmaxf(m_run, m_tile);
@@ -302,24 +306,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         alpha = ex2(m_run - m_new);  // 0 on the first tile (m_run = -inf)
         m_run = m_new;
       }
-      // P = 2^(s * scale_log2 - m) -> packed 16-bit pairs over the S columns
-      float sum0 = 0.f, sum1 = 0.f;
+      // P = 2^(s * scale_log2 - m): scale-and-shift and the row sum on packed f32x2
+      // pairs; exponentials on MUFU except one in eight on the FMA pipe. Masked keys
+      // (-inf) give exact zeros on both paths. P is written as 16-bit pairs over the
+      // S columns.
+      const uint64_t scale2 = f2_pack(scale_log2, scale_log2);
+      const uint64_t neg_m2 = f2_pack(-m_run, -m_run);
+      uint64_t sum2a = f2_pack(0.f, 0.f), sum2b = sum2a;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t packed[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int k = c * 32 + 2 * i;
-          const float a = fmaf(s[k], scale_log2, -m_run);
-          const float bb = fmaf(s[k + 1], scale_log2, -m_run);
+          const uint64_t x2 = f2_fma(f2_pack(s[k], s[k + 1]), scale2, neg_m2);
+          float a, b;
+          f2_unpack(x2, a, b);
           const float pa = ex2(a);
-          const float pb = (i & 1) ? ex2_poly(bb) : ex2(bb);  // 1 in 4 on the FMA pipe
-          sum0 += pa;
-          sum1 += pb;
+          const float pb = (i & 3) == 3 ? ex2_poly(b) : ex2(b);  // ex2_poly(-inf) = 0 too
+          if (i & 1) sum2b = f2_add(sum2b, f2_pack(pa, pb));
+          else sum2a = f2_add(sum2a, f2_pack(pa, pb));
           packed[i] = Elem<T>::pack2(pa, pb);
         }
         tmem_st16(lane_addr + s_col + c * 16, packed);
       }
+      float sa0, sa1, sb0, sb1;
+      f2_unpack(sum2a, sa0, sa1);
+      f2_unpack(sum2b, sb0, sb1);
+      const float sum0 = sa0 + sb0, sum1 = sa1 + sb1;
       l_run = l_run * alpha + (sum0 + sum1);
       if (moves && j > 0) {  // O_x is stable: PV_x(j-1) completed before S_x(j) did
 #pragma unroll
