@@ -57,11 +57,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+
 
 // Bounded wait for the phase with the given parity to complete. `abort` is a
 // CTA-shared flag: once any wait of the CTA has given up, later waits return at

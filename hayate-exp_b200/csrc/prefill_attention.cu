@@ -8,28 +8,30 @@
 // Work unit: one CTA per (128 consecutive query positions, pair of query heads of
 // one KV group, request). The two heads are two 128-row tiles, A and B, that see the
 // same keys under the same causal mask, so every K/V tile loaded serves both.
-// 320 threads, warp-specialised:
-//   warps 0-3 / 4-7 (softmax warpgroups A / B): thread r owns query row r of its
-//     tile (TMEM lane r). Per 128-key tile it reads its S row (tcgen05.ld), masks
-//     `key <= cache_len + t`, keeps a stale running max unless the true one grows
-//     by more than 2^8 (then rescales its O row in TMEM; O / l stays exact), turns
-//     the row into P (scale-and-shift and row sums on packed f32x2 pairs, 7 of 8
-//     exponentials on MUFU and 1 of 8 on the FMA pipe via ex2_poly; masked keys
-//     give exact 0 on both), and writes P as packed bf16/f16
-//     back over its S columns (tcgen05.st). At the end it normalises its O row and
-//     stores it.
-//   warp 8 (producer): per 128-key tile looks the page up and TMA-loads K and V
+// 576 threads, warp-specialised:
+//   warps 0-15 (softmax): warps 0-7 handle tile A and 8-15 tile B, both at once.
+//     In a tile, warps w and w + 4 own rows 32 * (w % 4) .. + 31 (TMEM lanes) and
+//     split the 128 key columns, exchanging row maxima through shared memory. Per
+//     tile a thread reads its 64 scores (tcgen05.ld), masks `key <= cache_len + t`,
+//     keeps a stale running max unless the true one grows by more than 2^8 (then
+//     rescales its O half-row in TMEM; O / l stays exact), turns the scores into P
+//     (scale-and-shift and row sums on packed f32x2 pairs, 7 of 8 exponentials on
+//     MUFU and 1 of 8 on the FMA pipe via ex2_poly; masked keys give exact 0 on
+//     both) and writes P as packed bf16/f16 back over its S columns (tcgen05.st).
+//     At the end the pair adds its row sums and each warp normalises and stores
+//     its half of the O rows.
+//   warp 16 (producer): per 128-key tile looks the page up and TMA-loads K and V
 //     (2 boxes of [128 tokens x 64 dims] each, 128B swizzle) into 2-stage rings.
-//   warp 9 (MMA issuer, one thread): S_x = Q_x K^T (M=128, N=128, 8 x K=16) and
+//   warp 17 (MMA issuer, one thread): S_x = Q_x K^T (M=128, N=128, 8 x K=16) and
 //     O_x += P_x V with P read straight from TMEM (tcgen05.mma, A in TMEM) and V as an
 //     MN-major shared-memory operand. Issue order per key tile j:
 //       PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1)
-//     so warpgroup A's softmax of tile j+1 overlaps the tensor core working on B
-//     and vice versa. tcgen05.mma ops of one thread execute in issue order, which
+//     so the softmax of tile A overlaps the tensor core working on B and vice
+//     versa. tcgen05.mma ops of one thread execute in issue order, which
 //     is what lets QK_x(j+1) overwrite the columns PV_x(j) reads P from, and makes
 //     O_x stable whenever S_x(j) is (its commit covers PV_x(j-1)).
 // TMEM (512 columns): S_A/P_A [0,128), S_B/P_B [128,256), O_A [256,384), O_B [384,512).
-// Shared memory: Q_A, Q_B 32 KB each, K and V 2 x 32 KB each (192 KB).
+// Shared memory: Q_A, Q_B 32 KB each, K and V 2 x 32 KB each (192 KB), 6 KB exchange.
 //
 // FLOPs per launch counted by the roofline: 4 * H_q * 128 per causal-valid
 // (query, key) pair.
@@ -45,16 +47,17 @@ namespace {
 constexpr int kRows = 128;  // query positions per CTA (per tile)
 constexpr int kKeys = 128;  // keys per KV tile
 constexpr int kD = 128;
-constexpr int kSoftmaxThreads = 256;
-constexpr int kProducerWarp = 8, kMmaWarp = 9;
-constexpr int kThreads = 320;
+constexpr int kSoftmaxThreads = 512;  // 8 warps per tile
+constexpr int kProducerWarp = 16, kMmaWarp = 17;
+constexpr int kThreads = 576;
 constexpr int kTileBytes = kRows * kD * 2;   // 32 KB
 constexpr int kChunkBytes = kTileBytes / 2;  // [128 rows x 64 elements]
 constexpr int kQOff = 0;                     // Q_A, Q_B
 constexpr int kKOff = kQOff + 2 * kTileBytes;
 constexpr int kVOff = kKOff + 2 * kTileBytes;
 constexpr int kBarOff = kVOff + 2 * kTileBytes;
-constexpr int kSmemBytes = kBarOff + 256 + 1024;
+constexpr int kRedOff = kBarOff + 256;       // row-max and row-sum exchange, 6 KB
+constexpr int kSmemBytes = kRedOff + 6 * 2 * 128 * 4 + 1024;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kOCol = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -70,6 +73,38 @@ __device__ __forceinline__ uint32_t sw128_offset(int r, int chunk) {
   return uint32_t((chunk >> 3) * kChunkBytes + r * 128 + (((chunk & 7) ^ (r & 7)) << 4));
 }
 
+// P = 2^(s * scale_log2 - m) for one thread's 64 scores, written to TMEM as 32
+// packed 16-bit pairs at `p_addr`; returns the row-sum contribution. Scale-and-shift
+// and the sum run on packed f32x2 pairs; 7 of 8 exponentials on MUFU (ex2), 1 of 8
+// on the FMA pipe (ex2_poly). Masked scores (-inf) give exact zeros on both paths.
+template <typename T>
+__device__ __forceinline__ float exp_tile(const float (&s)[64], uint64_t scale2, float m,
+                                          uint32_t p_addr) {
+  const uint64_t neg_m2 = f2_pack(-m, -m);
+  uint64_t sum2a = f2_pack(0.f, 0.f), sum2b = sum2a;
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    uint32_t packed[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int k = c * 32 + 2 * i;
+      const uint64_t x2 = f2_fma(f2_pack(s[k], s[k + 1]), scale2, neg_m2);
+      float a, b;
+      f2_unpack(x2, a, b);
+      const float pa = ex2(a);
+      const float pb = (i & 3) == 3 ? ex2_poly(b) : ex2(b);
+      if (i & 1) sum2b = f2_add(sum2b, f2_pack(pa, pb));
+      else sum2a = f2_add(sum2a, f2_pack(pa, pb));
+      packed[i] = Elem<T>::pack2(pa, pb);
+    }
+    tmem_st16(p_addr + c * 16, packed);
+  }
+  float sa0, sa1, sb0, sb1;
+  f2_unpack(sum2a, sa0, sa1);
+  f2_unpack(sum2b, sb0, sb1);
+  return (sa0 + sb0) + (sa1 + sb1);
+}
+
 struct Barriers {
   uint64_t q_full;
   uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
@@ -80,9 +115,9 @@ struct Barriers {
 };
 static_assert(sizeof(Barriers) <= 256, "barrier block");
 
-// 168 registers: 10 warps over 4 sub-partitions put 3 warps on one 16K-register file.
+// 96 registers: 18 warps over 4 sub-partitions put 5 warps on one 16K-register file.
 template <typename T>
-__global__ void __maxnreg__(168)
+__global__ void __maxnreg__(96)
     prefill_attention_kernel(const __grid_constant__ CUtensorMap k_map,
                              const __grid_constant__ CUtensorMap v_map,
                              const PrefillKernelParams P) {
@@ -141,7 +176,7 @@ __global__ void __maxnreg__(168)
       mbar_init(&bars->v_full[s], 1);
       mbar_init(&bars->v_empty[s], 1);
       mbar_init(&bars->s_full[s], 1);
-      mbar_init(&bars->p_full[s], kRows);
+      mbar_init(&bars->p_full[s], kSoftmaxThreads / 2);
     }
     mbar_init(&bars->o_done, 1);
     mbar_init(&bars->drain, 1);
@@ -245,60 +280,73 @@ __global__ void __maxnreg__(168)
       mbar_drain(&bars->drain, 0);
     }
   } else {
-    // ------------------------------------------------------------ softmax warpgroups
-    const int x = warp >> 2;                   // tile: 0 = A, 1 = B
-    const int r = threadIdx.x - x * kRows;     // query row == TMEM lane
-    const int h = h0 + x;
+    // ------------------------------------------------------------ softmax warps
+    // Warps 0-7 handle tile A and warps 8-15 tile B, both at once. Within a tile,
+    // warps w and w + 4 own rows 32 * (w % 4) .. + 31 (TMEM lanes) and split the 128
+    // key columns, exchanging row maxima through shared memory; row sums are added
+    // once, in the epilogue. Each sub-partition thus runs four softmax warps.
+    const int x = warp >> 3, half = (warp >> 2) & 1, quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // query row == TMEM lane
     const int t = t0 + r;
     const bool row_valid = t < p.query_len;
     const int limit = cache_len + min(t, p.query_len - 1);  // last visible key
-    const uint32_t lane_addr = tmem + (uint32_t((warp & 3) * 32) << 16);
-    const uint32_t s_col = x * 128, o_col = kOCol + x * 128;
+    const uint32_t lane_addr = tmem + (uint32_t(quarter * 32) << 16);
+    const int pair_bar = 1 + x * 4 + quarter;  // named barrier of the two warps of this row quarter
+    float* red_max = reinterpret_cast<float*>(smem + kRedOff) + x * (2 * 2 * kRows);  // [parity][half][row]
+    float* red_sum = reinterpret_cast<float*>(smem + kRedOff) + 2 * (2 * 2 * kRows) + x * (2 * kRows);
 
-    {  // Q row -> swizzled shared memory (zeros past the chunk)
-      const T* qrow = static_cast<const T*>(p.q) + b * p.q_sb + int64_t(h) * p.q_sh + int64_t(t) * p.q_st;
-      uint8_t* qdst = smem + kQOff + x * kTileBytes;
+    {  // Q rows -> swizzled shared memory: two threads per row, 8 chunks each
+      const int qx = threadIdx.x >> 8, qr = (threadIdx.x >> 1) & 127, qc = (threadIdx.x & 1) * 8;
+      const int qt = t0 + qr;
+      const T* qrow = static_cast<const T*>(p.q) + b * p.q_sb + int64_t(h0 + qx) * p.q_sh + int64_t(qt) * p.q_st;
+      uint8_t* qdst = smem + kQOff + qx * kTileBytes;
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
+      for (int c = qc; c < qc + 8; ++c) {
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (row_valid) v = reinterpret_cast<const uint4*>(qrow)[c];
-        *reinterpret_cast<uint4*>(qdst + sw128_offset(r, c)) = v;
+        if (qt < p.query_len) v = reinterpret_cast<const uint4*>(qrow)[c];
+        *reinterpret_cast<uint4*>(qdst + sw128_offset(qr, c)) = v;
       }
       fence_proxy_async_smem();
       mbar_arrive(&bars->q_full);
     }
 
     const float scale_log2 = p.scale * kLog2e;
+    const uint64_t scale2 = f2_pack(scale_log2, scale_log2);
+    const uint32_t s_col = x * 128 + half * 64;
+    const uint32_t p_col = x * 128 + half * 32;
+    const uint32_t o_col = kOCol + x * 128 + half * 64;
     float m_run = -INFINITY, l_run = 0.f;
     for (int j = 0; j < n_tiles; ++j) {
       mbar_wait(&bars->s_full[x], j & 1, err, abort);
       tc_fence_after();
-      float s[128];
+      float s[64];
       {
-        uint32_t raw[4][32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(lane_addr + s_col + c * 32, raw[c]);
+        uint32_t raw[2][32];
+        tmem_ld32(lane_addr + s_col, raw[0]);
+        tmem_ld32(lane_addr + s_col + 32, raw[1]);
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
           for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(raw[c][i]);
       }
-      // mask + row max on the raw scores (scale > 0 keeps the order)
-      const int key0 = j * kKeys;
-      const bool masked = key0 + kKeys - 1 > limit;  // only the diagonal tiles
-      if (masked) {
+      // mask + this half's row max on the raw scores (scale > 0 keeps the order)
+      const int key0 = j * kKeys + half * 64;
+      if (key0 + 63 > limit) {  // only the diagonal tiles
 #pragma unroll
-        for (int c = 0; c < 128; ++c)
+        for (int c = 0; c < 64; ++c)
           if (key0 + c > limit) s[c] = -INFINITY;
       }
       float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 128; c += 4) {
+      for (int c = 0; c < 64; c += 4) {
         mx0 = fmax3(mx0, s[c], s[c + 1]);
         mx1 = fmax3(mx1, s[c + 2], s[c + 3]);
       }
-      const float m_tile = fmaxf(mx0, mx1) * scale_log2;
+      float* slot = red_max + (j & 1) * 2 * kRows;
+      slot[half * kRows + r] = fmaxf(mx0, mx1);
+      named_bar_sync(pair_bar, 64);
+      const float m_tile = fmaxf(slot[r], slot[kRows + r]) * scale_log2;
       const float m_new = fmaxf(m_run, m_tile);
       const bool moves = __any_sync(0xffffffffu, m_new > m_run + kRescaleThreshold);
       float alpha = 1.f;
@@ -306,38 +354,11 @@ __global__ void __maxnreg__(168)
         alpha = ex2(m_run - m_new);  // 0 on the first tile (m_run = -inf)
         m_run = m_new;
       }
-      // P = 2^(s * scale_log2 - m): scale-and-shift and the row sum on packed f32x2
-      // pairs; exponentials on MUFU except one in eight on the FMA pipe. Masked keys
-      // (-inf) give exact zeros on both paths. P is written as 16-bit pairs over the
-      // S columns.
-      const uint64_t scale2 = f2_pack(scale_log2, scale_log2);
-      const uint64_t neg_m2 = f2_pack(-m_run, -m_run);
-      uint64_t sum2a = f2_pack(0.f, 0.f), sum2b = sum2a;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t packed[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int k = c * 32 + 2 * i;
-          const uint64_t x2 = f2_fma(f2_pack(s[k], s[k + 1]), scale2, neg_m2);
-          float a, b;
-          f2_unpack(x2, a, b);
-          const float pa = ex2(a);
-          const float pb = (i & 3) == 3 ? ex2_poly(b) : ex2(b);  // ex2_poly(-inf) = 0 too
-          if (i & 1) sum2b = f2_add(sum2b, f2_pack(pa, pb));
-          else sum2a = f2_add(sum2a, f2_pack(pa, pb));
-          packed[i] = Elem<T>::pack2(pa, pb);
-        }
-        tmem_st16(lane_addr + s_col + c * 16, packed);
-      }
-      float sa0, sa1, sb0, sb1;
-      f2_unpack(sum2a, sa0, sa1);
-      f2_unpack(sum2b, sb0, sb1);
-      const float sum0 = sa0 + sb0, sum1 = sa1 + sb1;
-      l_run = l_run * alpha + (sum0 + sum1);
+      const float tile_sum = exp_tile<T>(s, scale2, m_run, lane_addr + p_col);
+      l_run = l_run * alpha + tile_sum;
       if (moves && j > 0) {  // O_x is stable: PV_x(j-1) completed before S_x(j) did
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t o[32];
           tmem_ld32(lane_addr + o_col + c * 32, o);
           tmem_wait_ld();
@@ -351,13 +372,16 @@ __global__ void __maxnreg__(168)
       mbar_arrive(&bars->p_full[x]);
     }
 
-    // ---- epilogue: O / l -> out[b, h, t, :]
+    // ---- epilogue: O / l -> out[b, h0 + x, t, half * 64 ..]
+    red_sum[half * kRows + r] = l_run;
     mbar_wait(&bars->o_done, 0, err, abort);
     tc_fence_after();
-    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-    T* out = static_cast<T*>(p.out) + b * p.o_sb + int64_t(h) * p.o_sh + int64_t(t) * p.o_st;
+    named_bar_sync(pair_bar, 64);
+    const float l = red_sum[r] + red_sum[kRows + r];
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    T* out = static_cast<T*>(p.out) + b * p.o_sb + int64_t(h0 + x) * p.o_sh + int64_t(t) * p.o_st + half * 64;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 2; ++c) {
       uint32_t o[32];
       tmem_ld32(lane_addr + o_col + c * 32, o);
       tmem_wait_ld();
