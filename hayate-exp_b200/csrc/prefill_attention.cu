@@ -21,7 +21,8 @@
 //     At the end the pair adds its row sums and each warp normalises and stores
 //     its half of the O rows.
 //   warp 16 (producer): per 128-key tile looks the page up and TMA-loads K and V
-//     (2 boxes of [128 tokens x 64 dims] each, 128B swizzle) into 2-stage rings.
+//     (2 boxes of [128 tokens x 64 dims] each, 128B swizzle) into 2-stage rings,
+//     prefetching the tiles kPrefetchTiles ahead into L2.
 //   warp 17 (MMA issuer, one thread): S_x = Q_x K^T (M=128, N=128, 8 x K=16) and
 //     O_x += P_x V with P read straight from TMEM (tcgen05.mma, A in TMEM) and V as an
 //     MN-major shared-memory operand. Issue order per key tile j:
@@ -61,6 +62,7 @@ constexpr int kSmemBytes = kRedOff + 6 * 2 * 128 * 4 + 1024;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kOCol = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+constexpr int kPrefetchTiles = 4;          // L2 prefetch distance of the K/V stream
 
 struct PrefillKernelParams {
   AttentionParams a;
@@ -200,12 +202,23 @@ __global__ void __maxnreg__(96)
       tma_prefetch_desc(&k_map);
       tma_prefetch_desc(&v_map);
       const int plane = p.layer * p.num_kv_heads + g;
+      auto tile_row = [&](int j) {
+        const int tok = j * kKeys;
+        return (table[tok >> p.page_shift] << p.page_shift) + (tok & page_mask);
+      };
+      auto prefetch = [&](int j) {  // K and V of tile j into L2, kPrefetchTiles ahead of use
+        const int row = tile_row(j);
+        tma_prefetch_l2_3d(&k_map, 0, row, plane);
+        tma_prefetch_l2_3d(&k_map, 64, row, plane);
+        tma_prefetch_l2_3d(&v_map, 0, row, plane);
+        tma_prefetch_l2_3d(&v_map, 64, row, plane);
+      };
+      for (int j = 0; j < min(n_tiles, kPrefetchTiles); ++j) prefetch(j);
       for (int j = 0; j < n_tiles; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
-        const int tok = j * kKeys;
-        const int32_t page = table[tok >> p.page_shift];
-        const int row = (page << p.page_shift) + (tok & page_mask);
+        if (j + kPrefetchTiles < n_tiles) prefetch(j + kPrefetchTiles);
+        const int row = tile_row(j);
         if (j >= 2) mbar_wait(&bars->k_empty[st], ph ^ 1, err, abort);
         uint8_t* kdst = smem + kKOff + st * kTileBytes;
         mbar_arrive_expect_tx(&bars->k_full[st], kTileBytes);
@@ -227,24 +240,34 @@ __global__ void __maxnreg__(96)
     if (lane == 0) {
       constexpr uint32_t idesc_qk = umma_idesc_f16(kBf16, 128, 128, false, false);
       constexpr uint32_t idesc_pv = umma_idesc_f16(kBf16, 128, 128, false, true);
-      auto kmajor = [&](uint32_t base, int kk) {
-        return umma_desc_sw128(base + (kk >> 2) * kChunkBytes + (kk & 3) * 32, 16);
-      };
+      // Descriptor bases computed once: each MMA only adds a compile-time offset to
+      // the 14-bit start-address field (which cannot carry: shared memory < 256 KB),
+      // so one thread issues MMAs faster than the tensor core retires them.
+      const uint64_t q_desc0 = umma_desc_sw128(smem_base + kQOff, 16);
+      const uint64_t q_desc1 = umma_desc_sw128(smem_base + kQOff + kTileBytes, 16);
+      const uint64_t k_desc0 = umma_desc_sw128(smem_base + kKOff, 16);
+      const uint64_t k_desc1 = umma_desc_sw128(smem_base + kKOff + kTileBytes, 16);
+      const uint64_t v_desc0 = umma_desc_sw128(smem_base + kVOff, kChunkBytes);
+      const uint64_t v_desc1 = umma_desc_sw128(smem_base + kVOff + kTileBytes, kChunkBytes);
       auto issue_qk = [&](int x, int j) {  // S_x = Q_x K_j^T
-        const uint32_t qbase = smem_base + kQOff + x * kTileBytes;
-        const uint32_t kbase = smem_base + kKOff + (j & 1) * kTileBytes;
+        const uint64_t a0 = x ? q_desc1 : q_desc0, b0 = (j & 1) ? k_desc1 : k_desc0;
+        const uint32_t d = tmem + x * 128;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_f16_ss(tmem + x * 128, kmajor(qbase, kk), kmajor(kbase, kk), idesc_qk, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk) {
+          // k-step kk (16 elements): chunk kk / 4, 32-byte step inside the 128B atom
+          const uint64_t off = uint64_t(((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4);
+          umma_f16_ss(d, a0 + off, b0 + off, idesc_qk, kk > 0 ? 1u : 0u);
+        }
         umma_commit(&bars->s_full[x]);
       };
       auto issue_pv = [&](int x, int j) {  // O_x += P_x V_j, P_x in TMEM over S_x
-        const uint32_t vbase = smem_base + kVOff + (j & 1) * kTileBytes;
+        const uint64_t b0 = (j & 1) ? v_desc1 : v_desc0;
+        const uint32_t d = tmem + kOCol + x * 128, a = tmem + x * 128;
+        const uint32_t first = j > 0 ? 1u : 0u;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t vdesc = umma_desc_sw128(vbase + kk * 2048, kChunkBytes);
-          umma_f16_ts(tmem + kOCol + x * 128, tmem + x * 128 + kk * 8, vdesc, idesc_pv,
-                      (j > 0 || kk > 0) ? 1u : 0u);
+          // V is [keys x dims]: K-dim = keys (16 per step = 2048 bytes), N = dims (LBO = chunk)
+          umma_f16_ts(d, a + kk * 8, b0 + uint64_t((kk * 2048) >> 4), idesc_pv, kk > 0 ? 1u : first);
         }
       };
       mbar_wait(&bars->q_full, 0, err, abort);
