@@ -391,6 +391,69 @@ int hyt_kv_scatter(const void* k_new, const void* v_new, const int64_t* new_stri
   return HYT_OK;
 }
 
+int hyt_norm_rope_scatter(const void* q, const void* k, const void* v, const int64_t* qkv_strides,
+                          const void* q_norm_weight, const void* k_norm_weight, float eps,
+                          const float* cos, const float* sin, int32_t rope_positions,
+                          void* q_out, const int64_t* q_out_strides, void* k_pool, void* v_pool,
+                          int32_t num_layers, int32_t layer, int64_t capacity_tokens,
+                          const int32_t* page_table, int32_t page_table_stride,
+                          const int32_t* cache_lens, int32_t batch, int32_t query_len,
+                          int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                          int32_t page_size, int32_t dtype, int32_t* error_word, void* stream) {
+  g_last_error.clear();
+  if (!q || !k || !v || !qkv_strides || !q_norm_weight || !k_norm_weight || !cos || !sin ||
+      !q_out || !q_out_strides || !k_pool || !v_pool || !page_table || !cache_lens)
+    return fail(HYT_ERR_INVALID, "null pointer argument");
+  Geometry g{num_layers, layer, capacity_tokens, page_table_stride, batch, query_len,
+             num_q_heads, num_kv_heads, head_dim, page_size, dtype};
+  int rc = check_geometry(g);
+  if (rc != HYT_OK) return rc;
+  if (head_dim != 128) return fail(HYT_ERR_UNSUPPORTED, "fused norm/RoPE/scatter needs head_dim 128");
+  if (rope_positions < 1) return fail(HYT_ERR_INVALID, "rope_positions must be positive");
+  const int eb = elem_bytes(dtype);
+  const void* rows[4] = {q, k, v, q_out};
+  for (const void* r : rows)
+    if (reinterpret_cast<uintptr_t>(r) % (4 * eb)) return fail(HYT_ERR_INVALID, "q/k/v/q_out must be aligned to 4 elements");
+  for (int i = 0; i < 9; ++i)
+    if (qkv_strides[i] % 4) return fail(HYT_ERR_INVALID, "q/k/v strides must be multiples of 4 elements");
+  for (int i = 0; i < 3; ++i)
+    if (q_out_strides[i] % 4) return fail(HYT_ERR_INVALID, "q_out strides must be multiples of 4 elements");
+  if (reinterpret_cast<uintptr_t>(cos) % 16 || reinterpret_cast<uintptr_t>(sin) % 16)
+    return fail(HYT_ERR_INVALID, "cos/sin tables must be 16-byte aligned");
+  hyt::NormRopeParams p;
+  p.q = q;
+  p.q_sb = qkv_strides[0]; p.q_st = qkv_strides[1]; p.q_sh = qkv_strides[2];
+  p.k = k;
+  p.k_sb = qkv_strides[3]; p.k_st = qkv_strides[4]; p.k_sh = qkv_strides[5];
+  p.v = v;
+  p.v_sb = qkv_strides[6]; p.v_st = qkv_strides[7]; p.v_sh = qkv_strides[8];
+  p.q_out = q_out;
+  p.o_sb = q_out_strides[0]; p.o_sh = q_out_strides[1]; p.o_st = q_out_strides[2];
+  p.q_norm_weight = q_norm_weight;
+  p.k_norm_weight = k_norm_weight;
+  p.eps = eps;
+  p.cos = cos;
+  p.sin = sin;
+  p.rope_positions = rope_positions;
+  p.k_pool = k_pool;
+  p.v_pool = v_pool;
+  p.capacity = capacity_tokens;
+  p.layer = layer;
+  p.page_table = page_table;
+  p.page_table_stride = page_table_stride;
+  p.cache_lens = cache_lens;
+  p.batch = batch;
+  p.query_len = query_len;
+  p.num_q_heads = num_q_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.page_shift = log2_int(page_size);
+  p.num_pages = int32_t(capacity_tokens / page_size);
+  p.error_word = error_word;
+  cudaError_t err = hyt::run_norm_rope_scatter(p, dtype, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "norm/RoPE/scatter launch");
+  return HYT_OK;
+}
+
 int hyt_generic_attention(const void* q, const int64_t* q_strides, const void* k_pool,
                           const void* v_pool, int32_t num_layers, int32_t layer,
                           int64_t capacity_tokens, const int32_t* page_table,

@@ -63,4 +63,32 @@ cudaError_t run_decode_attention(const AttentionParams& p, const DecodeLaunch& d
 cudaError_t run_prefill_attention(const AttentionParams& p, const CUtensorMap& k_map,
                                   const CUtensorMap& v_map, int dtype, cudaStream_t stream);
 
+// ------------------------------------------------------------ fused QK-norm + RoPE + scatter
+struct NormRopeParams {
+  const void* q;  // [B, T, H_q, 128] element strides {b, t, h}
+  int64_t q_sb, q_st, q_sh;
+  const void* k;  // [B, T, H_kv, 128]
+  int64_t k_sb, k_st, k_sh;
+  const void* v;
+  int64_t v_sb, v_st, v_sh;
+  void* q_out;    // [B, H_q, T, 128] element strides {b, h, t}
+  int64_t o_sb, o_sh, o_st;
+  const void* q_norm_weight;
+  const void* k_norm_weight;
+  float eps;
+  const float* cos;  // [rope_positions, 128] fp32
+  const float* sin;
+  int32_t rope_positions;
+  void* k_pool;
+  void* v_pool;
+  int64_t capacity;
+  int32_t layer;
+  const int32_t* page_table;
+  int32_t page_table_stride;
+  const int32_t* cache_lens;
+  int32_t batch, query_len, num_q_heads, num_kv_heads, page_shift, num_pages;
+  int32_t* error_word;
+};
+cudaError_t run_norm_rope_scatter(const NormRopeParams& p, int dtype, cudaStream_t stream);
+
 }  // namespace hyt

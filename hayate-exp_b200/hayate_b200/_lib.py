@@ -38,6 +38,10 @@ SIGNATURES = {
     "hyt_decode_attention_noalloc": (ctypes.c_int, _ATTENTION_ARGS + [_c_i32, _c_i32, _c_p, _c_p]),
     "hyt_prefill_attention": (ctypes.c_int, _ATTENTION_ARGS + [_c_i32, _c_p, _c_p]),
     "hyt_generic_attention": (ctypes.c_int, _ATTENTION_ARGS + [_c_p, _c_p]),
+    "hyt_norm_rope_scatter": (ctypes.c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_f32, _c_p, _c_p,
+                                             _c_i32, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i64,
+                                             _c_p, _c_i32, _c_p, _c_i32, _c_i32, _c_i32, _c_i32,
+                                             _c_i32, _c_i32, _c_i32, _c_p, _c_p]),
     "hyt_attention_workspace_bytes": (_c_size, [_c_i32] * 8),
     "hyt_workspace_init": (ctypes.c_int, [_c_p, _c_size, _c_p]),
 }

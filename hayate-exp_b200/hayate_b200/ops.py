@@ -90,6 +90,50 @@ def kv_scatter(k_new: torch.Tensor, v_new: torch.Tensor, k_pool: torch.Tensor, v
     _lib.check(rc, "hyt_kv_scatter")
 
 
+def norm_rope_scatter(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_norm_weight: torch.Tensor,
+                      k_norm_weight: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                      k_pool: torch.Tensor, v_pool: torch.Tensor, layer: int, page_table: torch.Tensor,
+                      cache_lens: torch.Tensor, page_size: int, eps: float = 1e-6,
+                      q_out: torch.Tensor | None = None,
+                      error_word: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused QK-norm + RoPE + KV scatter: q/k/v are the projections ``[B, T, H, 128]``.
+
+    Returns ``q`` normalised and rotated as ``[B, H_q, T, 128]`` (backed by ``[B, T, H_q, 128]``
+    memory) and writes the normalised, rotated k and the raw v into the pools.
+    """
+    _require_cuda(q, k, v, q_norm_weight, k_norm_weight, cos, sin, k_pool, v_pool, page_table, cache_lens)
+    num_layers, num_kv_heads, capacity, head_dim = _pool_geometry(k_pool, v_pool)
+    if q.dim() != 4 or k.shape != v.shape or k.dim() != 4:
+        raise ValueError("q, k, v must be [batch, tokens, heads, head_dim]")
+    batch, query_len, num_q_heads, d = q.shape
+    if d != head_dim or k.shape[2] != num_kv_heads or k.shape[:2] != q.shape[:2]:
+        raise ValueError("q/k/v shapes do not match the pools")
+    for t in (q, k, v, q_norm_weight, k_norm_weight):
+        if t.dtype != k_pool.dtype:
+            raise ValueError("q/k/v and the norm weights must have the pool dtype")
+    if cos.dtype != torch.float32 or sin.dtype != torch.float32 or not (cos.is_contiguous() and sin.is_contiguous()):
+        raise ValueError("cos/sin must be contiguous fp32 [positions, head_dim] tables")
+    for t, name in ((q, "q"), (k, "k"), (v, "v")):
+        if t.stride(3) != 1:
+            raise ValueError(f"{name} must have a contiguous last dimension")
+    if q_out is None:
+        q_out = torch.empty((batch, query_len, num_q_heads, head_dim), dtype=q.dtype,
+                            device=q.device).transpose(1, 2)
+    strides = _lib.int64_array([q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1),
+                                k.stride(2), v.stride(0), v.stride(1), v.stride(2)])
+    out_strides = _lib.int64_array(_bht_strides(q_out, "q_out"))
+    pts = _table_args(page_table, cache_lens, batch)
+    rc = _lib.lib().hyt_norm_rope_scatter(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), strides, q_norm_weight.data_ptr(),
+        k_norm_weight.data_ptr(), float(eps), cos.data_ptr(), sin.data_ptr(), cos.shape[0],
+        q_out.data_ptr(), out_strides, k_pool.data_ptr(), v_pool.data_ptr(), num_layers, layer,
+        capacity, page_table.data_ptr(), pts, cache_lens.data_ptr(), batch, query_len,
+        num_q_heads, num_kv_heads, head_dim, page_size, dtype_code(q.dtype), _ptr(error_word),
+        _stream_ptr())
+    _lib.check(rc, "hyt_norm_rope_scatter")
+    return q_out
+
+
 def attention_workspace_bytes(batch: int, query_len: int, num_q_heads: int, num_kv_heads: int,
                               head_dim: int, max_kv_len: int, dtype: torch.dtype,
                               split_tokens: int = 0) -> int:

@@ -9,7 +9,8 @@ Same public surface as ``hayate/engine/paged_cache.py``:
   ``MemoryError``);
 * ``begin_batch`` returns a ``PagedKVBatch`` exposing ``write_layer(layer, k, v)``,
   ``attend_layer(q, layer)``, ``cache_lens`` (int64, read by the model to place
-  RoPE positions), ``page_table`` and ``page_size`` (``:33-71``).
+  RoPE positions), ``page_table`` and ``page_size`` (``:33-71``), plus
+  ``prepare_layer`` (QK-norm + RoPE + ``write_layer`` fused in one launch).
 
 What changes underneath:
 
@@ -120,6 +121,22 @@ class PagedKVBatch:
             v = v.contiguous()
         ops.kv_scatter(k, v, self.k_cache, self.v_cache, layer_idx, self.page_table,
                        self.cache_lens_i32, self.page_size, error_word=self._manager.error_word)
+
+    def prepare_layer(self, layer_idx: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                      q_norm_weight: torch.Tensor, k_norm_weight: torch.Tensor,
+                      cos: torch.Tensor, sin: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+        """QK-norm, RoPE and ``write_layer`` fused in one launch.
+
+        ``q``/``k``/``v`` are the projections as ``[B, T, H, D]`` (before the transpose of
+        ``hayate/model/attention.py:66-68``); the K/V written to the pages are those the
+        unfused path (norm -> transpose -> RoPE -> ``write_layer``) writes. Returns the
+        rotated ``q`` as ``[B, H_q, T, D]``, ready for ``attend_layer``.
+        """
+        if q.shape[1] != self.query_len:
+            raise ValueError("q/k/v must carry query_len tokens")
+        return ops.norm_rope_scatter(q, k, v, q_norm_weight, k_norm_weight, cos, sin, self.k_cache,
+                                     self.v_cache, layer_idx, self.page_table, self.cache_lens_i32,
+                                     self.page_size, eps=eps, error_word=self._manager.error_word)
 
     def attend_layer(self, q: torch.Tensor, layer_idx: int) -> torch.Tensor:
         """Causal GQA attention of ``q`` ``[B, H_q, T, D]`` over this layer's paged K/V."""

@@ -147,6 +147,26 @@ int hyt_prefill_attention(const void* q, const int64_t* q_strides, const void* k
                           int32_t page_size, int32_t dtype, float scale, int32_t max_kv_len,
                           int32_t* error_word, void* stream);
 
+/*
+ * Fused QK-norm + RoPE + KV scatter (head_dim 128).
+ * Replaces, in hayate/model/attention.py:62-75, q_norm/k_norm (nn.RMSNorm over
+ * head_dim, attention.py:34-35), apply_rope_vectorized at position cache_lens[b] + t
+ * with the model's fp32 cos/sin tables (hayate/model/rope.py:31-47) and
+ * PagedKVBatch.write_layer (paged_cache.py:44-60), in one launch. Inputs are the
+ * projections before the transpose: q [B, T, H_q, 128], k/v [B, T, H_kv, 128] with
+ * element strides {b, t, h} (qkv_strides = q's 3, then k's, then v's). q_out is
+ * [B, H_q, T, 128] with strides {b, h, t}. cos/sin are [rope_positions, 128] fp32.
+ */
+int hyt_norm_rope_scatter(const void* q, const void* k, const void* v, const int64_t* qkv_strides,
+                          const void* q_norm_weight, const void* k_norm_weight, float eps,
+                          const float* cos, const float* sin, int32_t rope_positions,
+                          void* q_out, const int64_t* q_out_strides, void* k_pool, void* v_pool,
+                          int32_t num_layers, int32_t layer, int64_t capacity_tokens,
+                          const int32_t* page_table, int32_t page_table_stride,
+                          const int32_t* cache_lens, int32_t batch, int32_t query_len,
+                          int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                          int32_t page_size, int32_t dtype, int32_t* error_word, void* stream);
+
 /* CUDA-core kernel only (any dtype, head_dim a multiple of 8 up to 256). */
 int hyt_generic_attention(const void* q, const int64_t* q_strides, const void* k_pool,
                           const void* v_pool, int32_t num_layers, int32_t layer,

@@ -262,3 +262,62 @@ def test_prefill_flags_bad_page_ids():
     torch.cuda.synchronize()
     assert int(err.item()) & 1
     assert float(out.float().abs().max()) == 0.0  # refused CTAs write zeros
+
+
+def reference_norm_rope(x: torch.Tensor, weight: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                        positions: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """The unfused path: nn.RMSNorm over head_dim, transpose, rope.py's half-split rotation."""
+    x = torch.nn.functional.rms_norm(x, (x.shape[-1],), weight, eps).transpose(1, 2)  # [B, H, T, D]
+    half = x.shape[-1] // 2
+    c = cos[positions].unsqueeze(1)
+    s = sin[positions].unsqueeze(1)
+    rotated = torch.cat((-x[..., half:], x[..., :half]), dim=-1)
+    return (x * c + rotated * s).to(x.dtype)
+
+
+@pytest.mark.parametrize("query_len", [1, 3, 130])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=str)
+def test_fused_norm_rope_scatter_matches_unfused_path(query_len, dtype):
+    lengths = [0, 127, 300]
+    gen = torch.Generator(device="cuda").manual_seed(query_len)
+    pages = sum(math.ceil((n + query_len) / 128) for n in lengths) + 2
+    managers = []
+    for _ in range(2):
+        m = PagedKVCacheManager(2, 8, 128, pages * 128, 128, len(lengths), dtype, "cuda")
+        W.shuffle_free_pages(m, 1)
+        hs = [m.allocate() for _ in lengths]
+        for h, n in zip(hs, lengths):
+            m.reserve(h, n)
+            h.length = n
+        managers.append((m, hs))
+    B, T = len(lengths), query_len
+    q = torch.randn(B, T, 32, 128, generator=gen, device="cuda").to(dtype)
+    k = torch.randn(B, T, 8, 128, generator=gen, device="cuda").to(dtype)
+    v = torch.randn(B, T, 8, 128, generator=gen, device="cuda").to(dtype)
+    wq = (1 + 0.1 * torch.randn(128, generator=gen, device="cuda")).to(dtype)
+    wk = (1 + 0.1 * torch.randn(128, generator=gen, device="cuda")).to(dtype)
+    cos, sin = W.rope_angles(torch.arange(8192, device="cuda"), 128)
+    cos, sin = cos.contiguous(), sin.contiguous()
+    positions = torch.tensor(lengths, device="cuda")[:, None] + torch.arange(T, device="cuda")[None, :]
+
+    (m0, h0), (m1, h1) = managers
+    b0 = m0.begin_batch(h0, T)
+    q_ref = reference_norm_rope(q, wq, cos, sin, positions)
+    k_ref = reference_norm_rope(k, wk, cos, sin, positions)
+    b0.write_layer(1, k_ref, v.transpose(1, 2))
+    b1 = m1.begin_batch(h1, T)
+    q_fused = b1.prepare_layer(1, q, k, v, wq, wk, cos, sin)
+    torch.cuda.synchronize()
+    m1.check_device_errors()
+    assert q_fused.shape == q_ref.shape
+    assert (q_fused.float() - q_ref.float()).abs().max().item() <= 2e-2
+    assert torch.equal(m0.v_cache, m1.v_cache)  # v is a byte copy
+    assert (m0.k_cache.float() - m1.k_cache.float()).abs().max().item() <= 2e-2
+    # same rounding steps as the unfused path: nearly every element agrees bit for bit
+    same = (q_fused == q_ref).float().mean().item()
+    assert same > 0.99, same
+    # and attention over the fused writes equals attention over the unfused ones
+    out0 = b0.attend_layer(q_ref, 1)
+    out1 = b1.attend_layer(q_fused, 1)
+    torch.cuda.synchronize()
+    assert (out0.float() - out1.float()).abs().max().item() <= 2e-2
