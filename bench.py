@@ -103,6 +103,10 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            deadline = time.time() + 3.0  # let nvidia-smi start so the timed region is sampled
+            while not self.lines and time.time() < deadline and self.proc.poll() is None:
+                time.sleep(0.02)
+            self.lines.clear()
         except OSError:
             self.proc = None
         return self

@@ -18,9 +18,11 @@ What changes underneath:
   launch of the decode, prefill or CUDA-core attention kernel. There is no
   block mask and no ``physical_to_logical`` table: the kernels walk the page
   table and apply the causal rule ``key <= cache_len + t`` themselves.
-* The per-step metadata (int64 and int32 lengths plus an int32 page table only
-  as wide as the batch's longest request) is packed into one host buffer and
-  uploaded with a single host-to-device copy, instead of one copy per request.
+* Page tables persist per request slot on the device: a step uploads only the
+  rows whose pages changed (usually none while decoding inside a page), its
+  lengths and slot ids in one small copy, and gathers its ``[B, W]`` int32 table
+  (``W`` = pages of the longest request) on the device, instead of one copy per
+  request plus a block mask.
 * Pages carry reference counts, so ``share`` can alias a prefix's physical
   pages into another request (prefix-cache page sharing). ``release`` and
   ``truncate`` decrement; a page returns to the free list at zero. A write that
@@ -91,6 +93,73 @@ class _MetaUploader:
         event.record()
         self.events[i] = event
         return dev
+
+
+class _SlotPageTable:
+    """Page-table rows kept per request slot, on the host and on the device.
+
+    Row ``s`` lists slot ``s``'s physical pages in logical order (-1 past the end).
+    The manager updates a row whenever that request's pages change; ``flush`` uploads
+    only the rows changed since the previous step (one packed copy plus a device
+    row copy), and ``gather`` builds a step's ``[B, W]`` table on the device from the
+    batch's slots. A decode step that crosses no page boundary uploads no row at all.
+    """
+
+    def __init__(self, max_requests: int, device: torch.device, width: int = 64):
+        self.device = device
+        self.host = np.full((max_requests, width), -1, dtype=np.int32)
+        self.count = np.zeros(max_requests, dtype=np.int64)
+        self.dirty: set[int] = set()
+        self.dev = torch.full((max_requests, width), -1, dtype=torch.int32, device=device)
+        self.uploader = _MetaUploader(device)
+
+    def _ensure_width(self, needed: int) -> None:
+        width = self.host.shape[1]
+        if needed <= width:
+            return
+        grown = max(needed, 2 * width)
+        host = np.full((self.host.shape[0], grown), -1, dtype=np.int32)
+        host[:, :width] = self.host
+        self.host = host
+        self.dev = torch.full((self.host.shape[0], grown), -1, dtype=torch.int32, device=self.device)
+        self.dirty.update(int(s) for s in np.nonzero(self.count)[0])
+
+    def set_row(self, slot: int, pages: Sequence[int]) -> None:
+        n = len(pages)
+        self._ensure_width(n)
+        old = int(self.count[slot])
+        if n:
+            self.host[slot, :n] = pages
+        if old > n:
+            self.host[slot, n:old] = -1
+        self.count[slot] = n
+        self.dirty.add(slot)
+
+    def append(self, slot: int, pages: Sequence[int]) -> None:
+        start = int(self.count[slot])
+        end = start + len(pages)
+        self._ensure_width(end)
+        self.host[slot, start:end] = pages
+        self.count[slot] = end
+        self.dirty.add(slot)
+
+    def set_entry(self, slot: int, index: int, page: int) -> None:
+        self.host[slot, index] = page
+        self.dirty.add(slot)
+
+    def flush(self) -> None:
+        if not self.dirty:
+            return
+        rows = np.fromiter(sorted(self.dirty), dtype=np.int32, count=len(self.dirty))
+        self.dirty.clear()
+        width = self.host.shape[1]
+        packed = np.concatenate([rows, self.host[rows].reshape(-1)])
+        dev = self.uploader.upload(packed)
+        n = len(rows)
+        self.dev.index_copy_(0, dev[:n].long(), dev[n:].view(n, width))
+
+    def gather(self, slots: torch.Tensor, width: int) -> torch.Tensor:
+        return self.dev[:, :width].index_select(0, slots)
 
 
 class PagedKVBatch:
@@ -180,6 +249,7 @@ class PagedKVCacheManager:
         self.error_word = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._workspace: torch.Tensor | None = None
         self._uploader = _MetaUploader(self.device)
+        self._rows = _SlotPageTable(max_requests, self.device)
         self.kernel = "auto"     # pin a kernel ("decode", "prefill", "generic") for testing
         self.split_tokens = 0    # 0 lets the library pick the decode split size
 
@@ -221,7 +291,9 @@ class PagedKVCacheManager:
             raise MemoryError(
                 f"paged KV cache is full: need {missing} additional pages, "
                 f"but only {len(self._free_pages)} remain")
-        handle.pages.extend(self._take_pages(missing))
+        new_pages = self._take_pages(missing)
+        handle.pages.extend(new_pages)
+        self._rows.append(handle.slot, new_pages)
 
     def share(self, source: PagedCacheHandle, num_tokens: int) -> PagedCacheHandle:
         """New handle whose first ``num_tokens`` alias ``source``'s physical pages.
@@ -239,6 +311,7 @@ class PagedKVCacheManager:
             self._page_refs[page] += 1
         handle.pages = list(pages)
         handle.length = num_tokens
+        self._rows.set_row(handle.slot, handle.pages)
         return handle
 
     def _make_writable(self, handle: PagedCacheHandle, first: int, last: int) -> None:
@@ -257,6 +330,7 @@ class PagedKVCacheManager:
                 pool[:, :, :, new * size:(new + 1) * size].copy_(pool[:, :, :, old * size:(old + 1) * size])
             self._drop_pages([old])
             handle.pages[logical] = new
+            self._rows.set_entry(handle.slot, logical, new)
 
     def allocate_for_request(self, cache=None) -> PagedCacheHandle:
         """Allocate a request handle and optionally import a contiguous prefix."""
@@ -293,6 +367,8 @@ class PagedKVCacheManager:
         dropped = handle.pages[keep:]
         handle.pages = handle.pages[:keep]
         self._drop_pages(dropped)
+        if dropped:
+            self._rows.set_row(handle.slot, handle.pages)
         handle.length = length
 
     def snapshot(self, handle: PagedCacheHandle, length: int | None = None) -> Cache:
@@ -313,6 +389,7 @@ class PagedKVCacheManager:
             return
         self._drop_pages(handle.pages)
         handle.pages.clear()
+        self._rows.set_row(handle.slot, ())
         handle.length = 0
         handle.released = True
         self._free_slots.append(handle.slot)
@@ -346,17 +423,18 @@ class PagedKVCacheManager:
             self._make_writable(handle, handle.length, handle.length + query_len - 1)
 
         batch = len(handles)
-        width = max(len(handle.pages) for handle in handles)
-        # one int32 upload: [cache_lens as int64 (2B words) | cache_lens int32 (B) | table (B x W)]
-        host = np.full(3 * batch + batch * width, -1, dtype=np.int32)
+        width = math.ceil(max(kv_lengths) / self.page_size)
+        # page-table rows that changed since the last step, then one small upload:
+        # [cache_lens as int64 (2B words) | cache_lens int32 (B) | slots (B)]
+        self._rows.flush()
+        host = np.empty(4 * batch, dtype=np.int32)
         host[: 2 * batch].view(np.int64)[:] = lengths
         host[2 * batch: 3 * batch] = lengths
-        table = host[3 * batch:].reshape(batch, width)
-        for row, handle in enumerate(handles):
-            table[row, : len(handle.pages)] = handle.pages
+        host[3 * batch:] = [handle.slot for handle in handles]
         meta = self._uploader.upload(host)
-        return PagedKVBatch(self, meta[3 * batch:].view(batch, width), meta[: 2 * batch].view(torch.int64),
-                            meta[2 * batch: 3 * batch], query_len, max(kv_lengths), meta)
+        table = self._rows.gather(meta[3 * batch:].long(), width)
+        return PagedKVBatch(self, table, meta[: 2 * batch].view(torch.int64),
+                            meta[2 * batch: 3 * batch], query_len, max(kv_lengths), (meta, table))
 
     def commit_batch(self, handles: Sequence[PagedCacheHandle], query_len: int) -> None:
         """Advance logical lengths after every layer wrote the step's K/V."""

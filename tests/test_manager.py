@@ -193,3 +193,26 @@ def test_kernels_refuse_cpu_tensors():
         batch.write_layer(0, torch.zeros(1, 1, 1, 4), torch.zeros(1, 1, 1, 4))
     with pytest.raises(RuntimeError, match="CUDA"):
         batch.attend_layer(torch.zeros(1, 1, 1, 4), 0)
+
+
+def test_persistent_page_table_tracks_every_page_change():
+    """The slot-indexed rows behind each step's page table follow every mutation."""
+    manager = PagedKVCacheManager(1, 1, 4, 64 * 128, 128, 6, torch.float32, "cpu")
+    values = torch.randn(1, 1, 300, 4)
+    a = manager.allocate_for_request(Cache.from_tensors(values, values))
+    b = manager.share(a, 200)                 # aliases a's first two pages
+    c = manager.allocate()
+    manager.reserve(c, 1000)                  # 8 pages, wider than the initial rows
+    c.length = 900
+    manager.truncate(c, 300)                  # drop pages 3..7
+    manager.release(manager.share(a, 256))    # a slot that comes and goes
+    d = manager.allocate()                    # reuses the released slot
+    handles = [a, b, c, d]
+    for step in range(3):
+        batch = manager.begin_batch(handles, 130)   # b's write lands in a shared page: COW
+        width = batch.page_table.shape[1]
+        for row, h in enumerate(handles):
+            expected = (h.pages + [-1] * width)[:width]
+            assert batch.page_table[row].tolist() == expected, (step, row)
+        manager.commit_batch(handles, 130)
+    assert manager.page_refcount(b.pages[1]) == 1 and b.pages[0] == a.pages[0]
