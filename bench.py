@@ -12,7 +12,9 @@ L2, so no flush is needed between steps.
 ``--workload prefill`` times config 3 (8 requests x 512-token chunk on a
 prefix U[0, 4096]); ``--workload longdecode`` times config 5 (512 requests x
 32768-token context in groups of 16 sharing a 4096-token prefix, split across
-ranks by group).
+ranks by group); ``--workload engine`` times config 4 (hayate's own engine and
+random-init Qwen3-4B from baseline/_ref, with this repo's KV manager, or with
+the reference's under ``--impl reference``).
 
 Multi-GPU: one process per GPU (torchrun), each rank owns its own pool and
 requests; there is no collective on the data path. Timing is by CUDA events,
@@ -51,7 +53,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "prefill", "longdecode"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "prefill", "longdecode", "engine"], default="decode")
     ap.add_argument("--split-tokens", type=int, default=0)
     ap.add_argument("--requests", type=int, default=64, help="decode requests per GPU (64 = config 2)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -539,6 +541,106 @@ def run_longdecode(args, world, rank, local, peaks, peak_kind):
     }
 
 
+# ---------------------------------------------------------------------------- engine (cfg 4)
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+ENGINE_REQUESTS, ENGINE_OUTPUT, ENGINE_POOL, ENGINE_BATCH = 256, 256, 262144, 48
+
+
+def engine_prompt_lengths(seed: int = 4, n: int = ENGINE_REQUESTS):
+    rng = np.random.RandomState(seed)
+    return np.clip(np.round(rng.lognormal(np.log(1024), 1.0, size=n)), 1, 8192).astype(int).tolist()
+
+
+class _StubTokenizer:
+    """The engine only decodes finished requests for display; ids are enough here."""
+
+    def decode(self, tokens, skip_special_tokens=True):
+        return ""
+
+
+def run_engine(args, world, rank, impl: str):
+    """hayate's own Engine and random-init Qwen3-4B (installed from the
+    reference into baseline/_ref), with only the paged KV manager swapped: this repo's
+    (impl "ours") or the reference's compiled-FlexAttention one (impl "reference")."""
+    import torch
+
+    if not os.path.isdir(os.path.join(REF_DIR, "hayate")):
+        return {"impl": impl, "workload": "engine",
+                "unavailable": "the reference engine is not installed in baseline/_ref"}
+    sys.path.insert(0, REF_DIR)
+    from hayate.engine import engine as ref_engine
+    from hayate.engine.request import Request
+    from hayate.engine.sampler import Sampler
+    from hayate.engine.scheduler import Scheduler
+    from hayate.model import Qwen3Model
+
+    if impl == "ours":
+        from hayate_b200 import PagedKVCacheManager as Manager
+    else:
+        from hayate.engine.paged_cache import PagedKVCacheManager as Manager
+
+    torch.manual_seed(0)
+    with torch.device("cuda"):
+        model = Qwen3Model()
+    model.initialize_rope("cuda")
+    model.eval()
+    eng = ref_engine.Engine.__new__(ref_engine.Engine)
+    eng.prefill_chunk_size = 512
+    eng.model = model
+    eng.num_layers, eng.num_kv_groups, eng.head_dim = model.num_layers, model.num_kv_groups, model.head_dim
+    eng.max_position_embeddings = model.max_position_embeddings
+    eng.tokenizer = _StubTokenizer()
+    eng.stop_token_ids = set()  # fixed-length generation (stop tokens disabled)
+    eng.scheduler = Scheduler(max_batch_size=ENGINE_BATCH)
+    eng.prefix_cache = None
+    eng.sampler = Sampler(eng.tokenizer, set())
+    eng.paged_cache = Manager(num_layers=eng.num_layers, num_kv_heads=eng.num_kv_groups,
+                              head_dim=eng.head_dim, max_cache_tokens=ENGINE_POOL, page_size=128,
+                              max_requests=ENGINE_BATCH, dtype=torch.bfloat16, device="cuda")
+    rng = np.random.RandomState(1234)
+
+    def submit(lengths, out_tokens):
+        reqs = []
+        for i, n in enumerate(lengths):
+            r = Request(id=i, prompt_tokens=rng.randint(0, 151936, size=n).tolist(), max_tokens=out_tokens)
+            eng._prepare_request(r)
+            eng.scheduler.add(r)
+            reqs.append(r)
+        return reqs
+
+    with torch.inference_mode():
+        # warm-up: library load / FlexAttention compilation on a few shapes
+        for _ in range(max(1, args.warmup)):
+            submit([700, 33, 1500, 129, 512, 1], 8)
+            while eng.generate():
+                pass
+        lengths = engine_prompt_lengths()
+        reqs = submit(lengths, ENGINE_OUTPUT)
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        start.record()
+        while eng.generate():
+            pass
+        end.record()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+    secs = start.elapsed_time(end) / 1e3
+    out_tokens = sum(len(r.tokens) for r in reqs)
+    prompt_tokens = int(sum(lengths))
+    return {
+        "impl": impl, "metric": "engine output tok/s (config 4)", "value": round(out_tokens / secs, 1),
+        "unit": "tok/s", "n_gpus": 1, "steps": 1, "warmup": args.warmup, "higher_is_better": True,
+        "total_tok_s": round((out_tokens + prompt_tokens) / secs, 1), "seconds": round(secs, 3),
+        "wall_seconds": round(wall, 3), "dtype": "bf16",
+        "data": "random-init Qwen3-4B weights, uniform random token ids, lognormal prompt lengths",
+        "config": {"workload": "config 4: hayate Engine, 256 requests, prompts lognormal(median 1024, max 8192), "
+                               "256 greedy tokens each, chunk 512, pool 262144 tokens",
+                   "max_batch": ENGINE_BATCH, "prompt_tokens": prompt_tokens, "output_tokens": out_tokens,
+                   "kv_manager": "hayate_b200" if impl == "ours" else "reference (torch.compile FlexAttention)"},
+    }
+
+
 # ---------------------------------------------------------------------------- reference arm
 def run_reference(args, world, rank):
     """CPU oracle on the host cores, same metric/unit/config as the GPU arm (rank 0 only)."""
@@ -594,6 +696,12 @@ def run_reference(args, world, rank):
 # ---------------------------------------------------------------------------- main
 def main():
     args = parse_args()
+    if args.workload == "engine":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        if rank == 0:
+            print(json.dumps(run_engine(args, world, rank, args.impl)), flush=True)
+        return
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))
