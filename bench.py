@@ -700,7 +700,15 @@ def main():
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))
         if rank == 0:
-            print(json.dumps(run_engine(args, world, rank, args.impl)), flush=True)
+            try:
+                result = run_engine(args, world, rank, args.impl)
+            except Exception as exc:  # the reference's torch.compile(flex_attention) path
+                if args.impl != "reference":
+                    raise
+                result = {"impl": "reference", "workload": "engine",
+                          "unavailable": f"reference GPU path failed: {type(exc).__name__}: "
+                                         f"{str(exc).splitlines()[0][:200]}"}
+            print(json.dumps(result), flush=True)
         return
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
