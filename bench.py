@@ -59,6 +59,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="headline workload only")
+    ap.add_argument("--reference-gpu", action="store_true",
+                    help="also time the reference's compiled FlexAttention path on the GPU (needs baseline/_ref)")
     return ap.parse_args()
 
 
@@ -298,6 +300,12 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
         "gpu_launches": 2 * args.steps,
         "clocks": clocks.summary(),
     }
+    if args.reference_gpu and rank == 0:
+        ref_gpu = reference_gpu_compare(manager, handles, q, k, v, out, kv_bytes / 1e9, "GB_s")
+        if "ms" in ref_gpu:
+            ref_gpu["ours_attention_ms"] = round(attn_ms, 4)
+            ref_gpu["speedup"] = round(ref_gpu["ms"] / attn_ms, 1)
+        result["reference_gpu"] = ref_gpu
     if not args.no_e2e:
         result["e2e"] = decode_e2e(args, world, manager, handles, ctx, q, k, v, step_bytes)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -433,7 +441,14 @@ def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=N
     step_ms = max_over_ranks(step_ms, world)
     total_flops = sum_over_ranks(float(flops), world)
     achieved = flops / (attn_ms / 1e3) / 1e12
+    ref_gpu = None
+    if args.reference_gpu and rank == 0:
+        ref_gpu = reference_gpu_compare(manager, handles, q, k, v, out, flops / 1e12, "TFLOP_s")
+        if "ms" in ref_gpu:
+            ref_gpu["ours_attention_ms"] = round(attn_ms, 4)
+            ref_gpu["speedup"] = round(ref_gpu["ms"] / attn_ms, 1)
     return {
+        "reference_gpu": ref_gpu,
         "workload": "config 3: bf16 chunked prefill, 8 requests x 512-token chunk on prefixes U[0, 4096]",
         "prefixes": prefixes, "value": round(total_flops / (step_ms / 1e3) / 1e12, 1), "unit": "TFLOP/s",
         "ms_per_step": round(step_ms, 4), "flops_per_step": flops,
@@ -539,6 +554,52 @@ def run_longdecode(args, world, rank, local, peaks, peak_kind):
         "gpu_launches": 2 * steps,
         "clocks": clocks.summary(),
     }
+
+
+# ---------------------------------------------------------------------------- reference GPU path
+def reference_gpu_compare(manager, handles, q, k, v, ours_out, per_step_units, unit, repeats=10):
+    """Time the reference's own paged attention on the GPU (torch.compile'd FlexAttention,
+    installed from the reference into baseline/_ref) on the same K/V and q, and compare its
+    output with ours. The reference pools are zeroed first: it allocates them with
+    torch.empty, and FlexAttention multiplies masked-out (zero-weight) keys' V rows too,
+    so uninitialised NaN bytes in the pool turn into NaN outputs."""
+    import torch
+
+    if not os.path.isdir(os.path.join(REF_DIR, "hayate")):
+        return {"unavailable": "the reference is not installed in baseline/_ref"}
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    try:
+        import hayate.engine.paged_cache as ref
+        from hayate.model.cache import Cache
+
+        T = q.shape[2]
+        rm = ref.PagedKVCacheManager(1, manager.num_kv_heads, manager.head_dim, manager.capacity_tokens,
+                                     manager.page_size, len(handles), torch.bfloat16, "cuda")
+        rm.k_cache.zero_()
+        rm.v_cache.zero_()
+        rhs = []
+        for h in handles:
+            snap = manager.snapshot(h)
+            rhs.append(rm.allocate_for_request(Cache.from_tensors(snap.k, snap.v) if h.length else None))
+        rb = rm.begin_batch(rhs, T)
+        with torch.inference_mode():
+            rb.write_layer(0, k.contiguous(), v.contiguous())
+            for _ in range(3):
+                out = rb.attend_layer(q.contiguous(), 0)
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(repeats):
+                out = rb.attend_layer(q.contiguous(), 0)
+            b.record()
+            torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / repeats
+        return {"ms": round(ms, 4), unit: round(per_step_units / (ms / 1e3), 3),
+                "max_abs_vs_ours": float((out.float() - ours_out.float()).abs().max().item()),
+                "path": "reference PagedKVBatch.attend_layer (torch.compile FlexAttention), same inputs"}
+    except Exception as exc:
+        return {"unavailable": f"{type(exc).__name__}: {str(exc).splitlines()[0][:200]}"}
 
 
 # ---------------------------------------------------------------------------- engine (cfg 4)

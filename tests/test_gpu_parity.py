@@ -321,3 +321,36 @@ def test_fused_norm_rope_scatter_matches_unfused_path(query_len, dtype):
     out1 = b1.attend_layer(q_fused, 1)
     torch.cuda.synchronize()
     assert (out0.float() - out1.float()).abs().max().item() <= 2e-2
+
+
+@pytest.mark.parametrize("prefix, own, query_len", [(4096, 300, 1), (256, 1000, 1), (384, 130, 40)])
+def test_shared_prefix_pages_attend_like_private_copies(prefix, own, query_len):
+    """Requests aliasing a prefix's pages (share) attend exactly like requests holding copies."""
+    gen = torch.Generator(device="cuda").manual_seed(prefix + own)
+    n_req = 3
+    pages = (math.ceil(prefix / 128) + math.ceil((own + query_len) / 128) + 1) * (n_req + 1) + 4
+    outs = []
+    for shared in (True, False):
+        g = torch.Generator(device="cuda").manual_seed(prefix + own)
+        m = PagedKVCacheManager(1, 8, 128, pages * 128, 128, n_req + 1, torch.bfloat16, "cuda")
+        W.shuffle_free_pages(m, 3)
+        root = m.allocate()
+        W.fill_history(m, root, prefix, g)
+        handles = []
+        for _ in range(n_req):
+            if shared:
+                h = m.share(root, prefix)
+            else:
+                h = m.allocate_for_request(m.snapshot(root))
+            W.fill_history(m, h, prefix + own, g, start=prefix)
+            handles.append(h)
+        m.release(root)
+        if shared:
+            assert all(m.page_refcount(p) == n_req for p in handles[0].pages[:prefix // 128])
+        q, k, v = W.step_inputs(m, handles, query_len, 32, g)
+        batch = m.begin_batch(handles, query_len)
+        batch.write_layer(0, k, v)
+        outs.append(batch.attend_layer(q, 0).clone())
+        torch.cuda.synchronize()
+        m.check_device_errors()
+    assert torch.equal(outs[0], outs[1])
