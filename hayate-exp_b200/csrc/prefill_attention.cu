@@ -22,10 +22,14 @@
 //     its half of the O rows.
 //   warp 16 (producer): per 128-key tile looks the page up and TMA-loads K and V
 //     (2 boxes of [128 tokens x 64 dims] each, 128B swizzle) into 2-stage rings,
-//     prefetching the tiles kPrefetchTiles ahead into L2.
-//   warp 17 (MMA issuer, one thread): S_x = Q_x K^T (M=128, N=128, 8 x K=16) and
-//     O_x += P_x V with P read straight from TMEM (tcgen05.mma, A in TMEM) and V as an
-//     MN-major shared-memory operand. Issue order per key tile j:
+//     prefetching the tile kPrefetchTiles ahead into L2.
+//   warp 17 (MMA issuer): S_x = Q_x K^T (M=128, N=128, 8 x K=16) and O_x += P_x V with
+//     P read straight from TMEM (tcgen05.mma, A in TMEM) and V as an MN-major
+//     shared-memory operand. The whole warp walks the loop and waits on the barriers;
+//     each group of MMAs and its commits is issued by the lane elect.sync picks at that
+//     site (lane 0, checked): on this B200 a warp-uniform elected issue costs ~39 cycles
+//     per MMA next to busy softmax warps, a lone-lane branch 67-95. Issue order per key
+//     tile j:
 //       PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1)
 //     so the softmax of tile A overlaps the tensor core working on B and vice
 //     versa. tcgen05.mma ops of one thread execute in issue order, which
@@ -62,7 +66,7 @@ constexpr int kSmemBytes = kRedOff + 6 * 2 * 128 * 4 + 1024;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kOCol = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
-constexpr int kPrefetchTiles = 4;          // L2 prefetch distance of the K/V stream
+constexpr int kPrefetchTiles = 3;          // L2 prefetch distance of the K/V stream (tiles)
 
 struct PrefillKernelParams {
   AttentionParams a;
@@ -206,18 +210,21 @@ __global__ void __maxnreg__(96)
         const int tok = j * kKeys;
         return (table[tok >> p.page_shift] << p.page_shift) + (tok & page_mask);
       };
-      auto prefetch = [&](int j) {  // K and V of tile j into L2, kPrefetchTiles ahead of use
+      auto prefetch = [&](int j) {  // K and V of tile j into L2
         const int row = tile_row(j);
         tma_prefetch_l2_3d(&k_map, 0, row, plane);
         tma_prefetch_l2_3d(&k_map, 64, row, plane);
         tma_prefetch_l2_3d(&v_map, 0, row, plane);
         tma_prefetch_l2_3d(&v_map, 64, row, plane);
       };
-      for (int j = 0; j < min(n_tiles, kPrefetchTiles); ++j) prefetch(j);
+      // Tiles 0 and 1 are loaded at once (both ring stages are free); from iteration 1 on,
+      // each iteration prefetches into L2 the tile kPrefetchTiles beyond the one it loads.
+      // No prefetch burst at start-up: the whole first wave loads Q and its first tiles
+      // then, sharing HBM.
       for (int j = 0; j < n_tiles; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
-        if (j + kPrefetchTiles < n_tiles) prefetch(j + kPrefetchTiles);
+        if (j >= 1 && j + kPrefetchTiles < n_tiles) prefetch(j + kPrefetchTiles);
         const int row = tile_row(j);
         if (j >= 2) mbar_wait(&bars->k_empty[st], ph ^ 1, err, abort);
         uint8_t* kdst = smem + kKOff + st * kTileBytes;
@@ -237,71 +244,81 @@ __global__ void __maxnreg__(96)
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc_qk = umma_idesc_f16(kBf16, 128, 128, false, false);
-      constexpr uint32_t idesc_pv = umma_idesc_f16(kBf16, 128, 128, false, true);
-      // Descriptor bases computed once: each MMA only adds a compile-time offset to
-      // the 14-bit start-address field (which cannot carry: shared memory < 256 KB),
-      // so one thread issues MMAs faster than the tensor core retires them.
-      const uint64_t q_desc0 = umma_desc_sw128(smem_base + kQOff, 16);
-      const uint64_t q_desc1 = umma_desc_sw128(smem_base + kQOff + kTileBytes, 16);
-      const uint64_t k_desc0 = umma_desc_sw128(smem_base + kKOff, 16);
-      const uint64_t k_desc1 = umma_desc_sw128(smem_base + kKOff + kTileBytes, 16);
-      const uint64_t v_desc0 = umma_desc_sw128(smem_base + kVOff, kChunkBytes);
-      const uint64_t v_desc1 = umma_desc_sw128(smem_base + kVOff + kTileBytes, kChunkBytes);
-      auto issue_qk = [&](int x, int j) {  // S_x = Q_x K_j^T
-        const uint64_t a0 = x ? q_desc1 : q_desc0, b0 = (j & 1) ? k_desc1 : k_desc0;
-        const uint32_t d = tmem + x * 128;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          // k-step kk (16 elements): chunk kk / 4, 32-byte step inside the 128B atom
-          const uint64_t off = uint64_t(((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4);
-          umma_f16_ss(d, a0 + off, b0 + off, idesc_qk, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&bars->s_full[x]);
-      };
-      auto issue_pv = [&](int x, int j) {  // O_x += P_x V_j, P_x in TMEM over S_x
-        const uint64_t b0 = (j & 1) ? v_desc1 : v_desc0;
-        const uint32_t d = tmem + kOCol + x * 128, a = tmem + x * 128;
-        const uint32_t first = j > 0 ? 1u : 0u;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          // V is [keys x dims]: K-dim = keys (16 per step = 2048 bytes), N = dims (LBO = chunk)
-          umma_f16_ts(d, a + kk * 8, b0 + uint64_t((kk * 2048) >> 4), idesc_pv, kk > 0 ? 1u : first);
-        }
-      };
-      mbar_wait(&bars->q_full, 0, err, abort);
-      mbar_wait(&bars->k_full[0], 0, err, abort);
-      tc_fence_after();
-      issue_qk(0, 0);
-      issue_qk(1, 0);
-      umma_commit(&bars->k_empty[0]);
-      for (int j = 0; j < n_tiles; ++j) {
-        const bool more = j + 1 < n_tiles;
-        mbar_wait(&bars->v_full[j & 1], (j >> 1) & 1, err, abort);
-        // tile A
-        mbar_wait(&bars->p_full[0], j & 1, err, abort);
-        tc_fence_after();
-        issue_pv(0, j);
-        if (more) {
-          mbar_wait(&bars->k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, err, abort);
+    // The whole warp walks the loop and waits on the barriers (descriptors stay
+    // warp-uniform); each group of tcgen05 ops and its commit is issued by one lane
+    // chosen by elect.sync at that site.
+    constexpr uint32_t idesc_qk = umma_idesc_f16(kBf16, 128, 128, false, false);
+    constexpr uint32_t idesc_pv = umma_idesc_f16(kBf16, 128, 128, false, true);
+    // all descriptors share their high halves (layout, SBO); the low halves hold the start
+    // address, which never carries into the high half (shared memory < 256 KB)
+    const uint64_t q_desc0 = umma_desc_sw128(smem_base + kQOff, 16);
+    const uint32_t hi = uint32_t(q_desc0 >> 32);
+    const uint32_t q_lo0 = uint32_t(q_desc0);
+    const uint32_t q_lo1 = uint32_t(umma_desc_sw128(smem_base + kQOff + kTileBytes, 16));
+    const uint32_t k_lo0 = uint32_t(umma_desc_sw128(smem_base + kKOff, 16));
+    const uint32_t k_lo1 = uint32_t(umma_desc_sw128(smem_base + kKOff + kTileBytes, 16));
+    const uint32_t v_lo0 = uint32_t(umma_desc_sw128(smem_base + kVOff, kChunkBytes));
+    const uint32_t v_lo1 = uint32_t(umma_desc_sw128(smem_base + kVOff + kTileBytes, kChunkBytes));
+    // self-check: an issuing block must run on exactly one lane, always the same one
+    // (lane 0), so that every commit covers every tcgen05 op issued before it
+    auto single_lane = [&]() {
+      if (__activemask() != (1u << lane) || lane != 0) {
+        flag_error(err, HYT_DEVERR_ISSUE_LANE);
+        return false;
+      }
+      return true;
+    };
+    // PV_x(j) (optional) then, if qk, S_x = Q_x K_{j+1}^T with its commit, one lane
+    auto issue = [&](int x, int j, bool pv, bool qk, uint64_t* extra_commit, uint64_t* extra_commit2) {
+      if (elect_one()) {
+        if (single_lane()) {
           tc_fence_after();
-          issue_qk(0, j + 1);
-        }
-        // tile B
-        mbar_wait(&bars->p_full[1], j & 1, err, abort);
-        tc_fence_after();
-        issue_pv(1, j);
-        umma_commit(&bars->v_empty[j & 1]);
-        if (more) {
-          issue_qk(1, j + 1);
-          umma_commit(&bars->k_empty[(j + 1) & 1]);
+          if (pv) {
+            const uint32_t b0 = (j & 1) ? v_lo1 : v_lo0;
+            const uint32_t d = tmem + kOCol + x * 128, a = tmem + x * 128;
+            const uint32_t first = j > 0 ? 1u : 0u;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              umma_f16_ts_lh(d, a + kk * 8, b0 + uint32_t((kk * 2048) >> 4), hi, idesc_pv, kk > 0 ? 1u : first);
+          }
+          if (qk) {
+            const int jq = pv ? j + 1 : j;
+            const uint32_t a0 = x ? q_lo1 : q_lo0, b0 = (jq & 1) ? k_lo1 : k_lo0;
+            const uint32_t d = tmem + x * 128;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint32_t off = uint32_t(((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4);
+              umma_f16_ss_lh(d, a0 + off, hi, b0 + off, hi, idesc_qk, kk > 0 ? 1u : 0u);
+            }
+            umma_commit(&bars->s_full[x]);
+          }
+          if (extra_commit != nullptr) umma_commit(extra_commit);
+          if (extra_commit2 != nullptr) umma_commit(extra_commit2);
         }
       }
-      umma_commit(&bars->o_done);
-      umma_commit(&bars->drain);  // every MMA done before TMEM is released
-      mbar_drain(&bars->drain, 0);
+      __syncwarp();
+    };
+    mbar_wait(&bars->q_full, 0, err, abort);
+    mbar_wait(&bars->k_full[0], 0, err, abort);
+    issue(0, 0, false, true, nullptr, nullptr);
+    issue(1, 0, false, true, &bars->k_empty[0], nullptr);
+    for (int j = 0; j < n_tiles; ++j) {
+      const bool more = j + 1 < n_tiles;
+      mbar_wait(&bars->v_full[j & 1], (j >> 1) & 1, err, abort);
+      mbar_wait(&bars->p_full[0], j & 1, err, abort);  // tile A
+      if (more) mbar_wait(&bars->k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, err, abort);
+      issue(0, j, true, more, nullptr, nullptr);
+      mbar_wait(&bars->p_full[1], j & 1, err, abort);  // tile B
+      issue(1, j, true, more, &bars->v_empty[j & 1], more ? &bars->k_empty[(j + 1) & 1] : nullptr);
     }
+    if (elect_one()) {
+      if (single_lane()) {
+        umma_commit(&bars->o_done);
+        umma_commit(&bars->drain);  // every MMA done before TMEM is released
+      }
+    }
+    __syncwarp();
+    mbar_drain(&bars->drain, 0);
   } else {
     // ------------------------------------------------------------ softmax warps
     // Warps 0-7 handle tile A and warps 8-15 tile B, both at once. Within a tile,

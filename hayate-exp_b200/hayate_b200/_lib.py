@@ -19,6 +19,7 @@ DEVICE_ERRORS = {
     2: "kv length needs more pages than the page table row holds",
     4: "kv length beyond the max_kv_len the launch was sized for",
     8: "a bounded pipeline wait gave up",
+    16: "tensor-core ops issued on other than exactly one lane (work skipped)",
 }
 
 _c_i32, _c_i64, _c_f32, _c_size, _c_p = (ctypes.c_int32, ctypes.c_int64, ctypes.c_float,

@@ -51,7 +51,8 @@ enum {
   HYT_DEVERR_PAGE_RANGE = 1,   /* page id outside [0, capacity_tokens / page_size) */
   HYT_DEVERR_TABLE_RANGE = 2,  /* kv_len needs more pages than page_table_stride */
   HYT_DEVERR_SPLIT_RANGE = 4,  /* kv_len > max_kv_len given at launch */
-  HYT_DEVERR_WAIT_TIMEOUT = 8  /* a bounded pipeline wait gave up */
+  HYT_DEVERR_WAIT_TIMEOUT = 8, /* a bounded pipeline wait gave up */
+  HYT_DEVERR_ISSUE_LANE = 16   /* tensor-core issue ran on other than exactly one lane (work skipped) */
 };
 
 /* Message of the last failed call on this thread ("" if none). */
