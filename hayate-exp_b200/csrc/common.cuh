@@ -96,7 +96,7 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
 }
 
 // ---------------------------------------------------------------- TMA
-// 3-D tiled load into shared memory, completing on an mbarrier (no multicast).
+// 3-D tiled load into this CTA's shared memory, completing on an mbarrier.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int c0, int c1, int c2) {
   asm volatile(
