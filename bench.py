@@ -59,6 +59,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="headline workload only")
+    ap.add_argument("--prefix-max", type=int, default=4096,
+                    help="prefill workload: prefixes drawn from U[0, prefix-max] (config 3: 4096)")
     ap.add_argument("--reference-gpu", action="store_true",
                     help="also time the reference's compiled FlexAttention path on the GPU (needs baseline/_ref)")
     return ap.parse_args()
@@ -395,8 +397,9 @@ def cpu_baseline_decode(manager, batch, q, ctx, budget_s: float = 10.0):
 
 
 # ---------------------------------------------------------------------------- prefill (cfg 3)
-def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=None):
-    """8 requests x 512-token chunk on prefixes U[0, 4096]; scatter + tcgen05 prefill attention."""
+def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=None, prefix_max=None):
+    """8 requests x 512-token chunk on prefixes U[0, prefix_max] (config 3: 4096); scatter +
+    tcgen05 prefill attention."""
     import torch
 
     import oracle
@@ -406,7 +409,8 @@ def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=N
     steps = args.steps if steps is None else steps
     warmup = args.warmup if warmup is None else warmup
     T = 512
-    prefixes = prefill_prefixes(2000 + rank)
+    prefix_max = args.prefix_max if prefix_max is None else prefix_max
+    prefixes = prefill_prefixes(2000 + rank, hi=prefix_max)
     pages = sum(math.ceil((n + T) / 128) for n in prefixes) + 8
     manager = PagedKVCacheManager(1, 8, 128, pages * 128, 128, len(prefixes), torch.bfloat16, "cuda")
     W.shuffle_free_pages(manager, 2000 + rank)
@@ -458,14 +462,16 @@ def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=N
             ref_gpu["speedup"] = round(ref_gpu["ms"] / attn_ms, 1)
     return {
         "reference_gpu": ref_gpu,
-        "workload": "config 3: bf16 chunked prefill, 8 requests x 512-token chunk on prefixes U[0, 4096]",
+        "workload": f"{'config 3' if prefix_max == 4096 else 'config 3 shape, longer prefixes'}: bf16 chunked "
+                    f"prefill, 8 requests x 512-token chunk on prefixes U[0, {prefix_max}]",
         "prefixes": prefixes, "value": round(total_flops / (step_ms / 1e3) / 1e12, 1), "unit": "TFLOP/s",
         "ms_per_step": round(step_ms, 4), "flops_per_step": flops,
         "attention_only": {"ms": round(attn_ms, 4), "TFLOP_s": round(achieved, 1)},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
                      "frac_of_sustained": round(achieved / peaks["bf16_tflops_sustained"], 4),
-                     "peak_source": f"{peak_kind} bf16_tflops (burst)", "traffic": PREFILL_CFG3_TRAFFIC,
+                     "peak_source": f"{peak_kind} bf16_tflops (burst)",
+                     "traffic": PREFILL_CFG3_TRAFFIC if prefix_max == 4096 else None,
                      "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + write.sum)",
                      "kernel": "prefill_attention_kernel (tcgen05 + TMEM)"},
         "l2": "256 MB buffer written between timed steps (L2 flush); events bracket each step",
@@ -796,7 +802,12 @@ def main():
         result = run_decode(args, world, rank, local, peaks, peak_kind)
         if not args.no_extras:
             # config 3 beside the headline (short: 50 timed steps)
-            result["prefill"] = run_prefill(args, world, rank, local, peaks, peak_kind, steps=50, warmup=5)
+            result["prefill"] = run_prefill(args, world, rank, local, peaks, peak_kind, steps=50, warmup=5,
+                                            prefix_max=4096)
+            # the config-3 launch is short (~0.2 ms); the same shape on longer prefixes shows
+            # the kernel's steady state
+            result["prefill_long_prefix"] = run_prefill(args, world, rank, local, peaks, peak_kind,
+                                                        steps=20, warmup=3, prefix_max=32768)
     elif args.workload == "prefill":
         result = run_prefill(args, world, rank, local, peaks, peak_kind)
     else:
