@@ -179,7 +179,30 @@ hyt::AttentionParams attention_params(const void* q, const int64_t* qs, const vo
   p.num_pages = int32_t(g.capacity / g.page_size);
   p.scale = scale;
   p.error_word = error_word;
+  p.q_start = nullptr;
+  p.q_len = nullptr;
+  p.req_ids = nullptr;
+  p.num_listed = 0;
+  p.total_tokens = 0;
   return p;
+}
+
+// Per-request addressing of a packed batch, and the request list one launch serves.
+struct PackedArgs {
+  const int32_t* q_start;
+  const int32_t* q_len;
+  const int32_t* req_ids;
+  int32_t num_listed;
+  int32_t total_tokens;
+};
+
+void apply_packed(hyt::AttentionParams& p, const PackedArgs* pk) {
+  if (pk == nullptr) return;
+  p.q_start = pk->q_start;
+  p.q_len = pk->q_len;
+  p.req_ids = pk->req_ids;
+  p.num_listed = pk->num_listed;
+  p.total_tokens = pk->total_tokens;
 }
 
 int check_attention_pointers(const void* q, const int64_t* qs, const void* k_pool,
@@ -245,13 +268,14 @@ int launch_decode(const void* q, const int64_t* qs, const void* k_pool, const vo
                   const Geometry& g, const int32_t* page_table, const int32_t* cache_lens,
                   void* out, const int64_t* os, float scale, int32_t max_kv_len,
                   int32_t split_tokens, void* workspace, size_t workspace_bytes,
-                  int32_t* error_word, cudaStream_t stream) {
+                  int32_t* error_word, cudaStream_t stream, const PackedArgs* pk = nullptr) {
   if (max_kv_len < g.query_len) return fail(HYT_ERR_INVALID, "max_kv_len must be >= query_len");
   if (split_tokens < 0) return fail(HYT_ERR_INVALID, "split_tokens must be >= 0");
-  const DecodeLayout L = decode_layout(g.batch, g.query_len, g.num_q_heads, g.num_kv_heads,
+  const int32_t count = pk != nullptr && pk->req_ids != nullptr ? pk->num_listed : g.batch;
+  const DecodeLayout L = decode_layout(count, g.query_len, g.num_q_heads, g.num_kv_heads,
                                        max_kv_len, split_tokens);
   if (L.max_splits > 65535) return fail(HYT_ERR_UNSUPPORTED, "too many splits for one launch");
-  if (g.batch > 65535 || g.num_kv_heads > 65535) return fail(HYT_ERR_UNSUPPORTED, "batch too large");
+  if (count > 65535 || g.num_kv_heads > 65535) return fail(HYT_ERR_UNSUPPORTED, "batch too large");
   if (L.total > 0 && (workspace == nullptr || workspace_bytes < L.total))
     return fail(HYT_ERR_WORKSPACE, "workspace missing or smaller than hyt_attention_workspace_bytes()");
   CUtensorMap k_map, v_map;
@@ -262,6 +286,7 @@ int launch_decode(const void* q, const int64_t* qs, const void* k_pool, const vo
   if (rc != HYT_OK) return rc;
   hyt::AttentionParams p = attention_params(q, qs, k_pool, v_pool, g, page_table, cache_lens,
                                             out, os, scale, error_word);
+  apply_packed(p, pk);
   hyt::DecodeLaunch d;
   d.split_tokens = L.split_tokens;
   d.max_splits = L.max_splits;
@@ -292,8 +317,9 @@ bool prefill_eligible(const Geometry& g, const void* q, const int64_t* qs, const
 int launch_prefill(const void* q, const int64_t* qs, const void* k_pool, const void* v_pool,
                    const Geometry& g, const int32_t* page_table, const int32_t* cache_lens,
                    void* out, const int64_t* os, float scale, int32_t* error_word,
-                   cudaStream_t stream) {
-  if (g.batch > 65535 || g.num_q_heads > 65535) return fail(HYT_ERR_UNSUPPORTED, "batch too large");
+                   cudaStream_t stream, const PackedArgs* pk = nullptr) {
+  const int32_t count = pk != nullptr && pk->req_ids != nullptr ? pk->num_listed : g.batch;
+  if (count > 65535 || g.num_q_heads > 65535) return fail(HYT_ERR_UNSUPPORTED, "batch too large");
   CUtensorMap k_map, v_map;
   const int64_t planes = int64_t(g.num_layers) * g.num_kv_heads;
   int rc = pool_tensor_map(k_pool, g.dtype, g.head_dim, g.capacity, planes, 128, &k_map);
@@ -302,6 +328,7 @@ int launch_prefill(const void* q, const int64_t* qs, const void* k_pool, const v
   if (rc != HYT_OK) return rc;
   hyt::AttentionParams p = attention_params(q, qs, k_pool, v_pool, g, page_table, cache_lens,
                                             out, os, scale, error_word);
+  apply_packed(p, pk);
   cudaError_t err = hyt::run_prefill_attention(p, k_map, v_map, g.dtype, stream);
   if (err != cudaSuccess) return cuda_fail(err, "prefill attention launch");
   return HYT_OK;
@@ -310,11 +337,12 @@ int launch_prefill(const void* q, const int64_t* qs, const void* k_pool, const v
 int launch_generic(const void* q, const int64_t* qs, const void* k_pool, const void* v_pool,
                    const Geometry& g, const int32_t* page_table, const int32_t* cache_lens,
                    void* out, const int64_t* os, float scale, int32_t* error_word,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, const PackedArgs* pk = nullptr) {
   if (g.head_dim % 8 || g.head_dim > 256)
     return fail(HYT_ERR_UNSUPPORTED, "head_dim must be a multiple of 8 and at most 256");
   hyt::AttentionParams p = attention_params(q, qs, k_pool, v_pool, g, page_table, cache_lens,
                                             out, os, scale, error_word);
+  apply_packed(p, pk);
   cudaError_t err = hyt::run_generic_attention(p, g.dtype, stream);
   if (err != cudaSuccess) return cuda_fail(err, "generic attention launch");
   return HYT_OK;
@@ -386,6 +414,9 @@ int hyt_kv_scatter(const void* k_new, const void* v_new, const int64_t* new_stri
   p.page_shift = log2_int(page_size);
   p.num_pages = int32_t(capacity_tokens / page_size);
   p.error_word = error_word;
+  p.q_start = nullptr;
+  p.token_request = nullptr;
+  p.total_tokens = 0;
   cudaError_t err = hyt::run_kv_scatter(p, elem_bytes(dtype), static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "kv scatter launch");
   return HYT_OK;
@@ -449,6 +480,9 @@ int hyt_norm_rope_scatter(const void* q, const void* k, const void* v, const int
   p.page_shift = log2_int(page_size);
   p.num_pages = int32_t(capacity_tokens / page_size);
   p.error_word = error_word;
+  p.q_start = nullptr;
+  p.token_request = nullptr;
+  p.total_tokens = 0;
   cudaError_t err = hyt::run_norm_rope_scatter(p, dtype, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "norm/RoPE/scatter launch");
   return HYT_OK;
@@ -596,6 +630,183 @@ int hyt_paged_attention(const void* q, const int64_t* q_strides, const void* k_p
                           out_strides, scale, error_word, s);
   return launch_generic(q, q_strides, k_pool, v_pool, g, page_table, cache_lens, out,
                         out_strides, scale, error_word, s);
+}
+
+int hyt_kv_scatter_packed(const void* k_new, const void* v_new, const int64_t* new_strides,
+                          void* k_pool, void* v_pool, int32_t num_layers, int32_t layer,
+                          int64_t capacity_tokens, const int32_t* page_table,
+                          int32_t page_table_stride, const int32_t* cache_lens,
+                          const int32_t* q_start, const int32_t* token_request, int32_t batch,
+                          int32_t total_tokens, int32_t num_kv_heads, int32_t head_dim,
+                          int32_t page_size, int32_t dtype, int32_t* error_word, void* stream) {
+  g_last_error.clear();
+  if (!k_new || !v_new || !new_strides || !k_pool || !v_pool || !page_table || !cache_lens ||
+      !q_start || !token_request)
+    return fail(HYT_ERR_INVALID, "null pointer argument");
+  if (total_tokens < 1) return fail(HYT_ERR_INVALID, "total_tokens must be positive");
+  Geometry g{num_layers, layer, capacity_tokens, page_table_stride, batch, 1,
+             num_kv_heads, num_kv_heads, head_dim, page_size, dtype};
+  int rc = check_geometry(g);
+  if (rc != HYT_OK) return rc;
+  hyt::ScatterParams p;
+  p.k_new = static_cast<const uint8_t*>(k_new);
+  p.v_new = static_cast<const uint8_t*>(v_new);
+  p.k_sb = 0;
+  p.k_st = new_strides[0];
+  p.k_sh = new_strides[1];
+  p.v_sb = 0;
+  p.v_st = new_strides[2];
+  p.v_sh = new_strides[3];
+  p.k_pool = static_cast<uint8_t*>(k_pool);
+  p.v_pool = static_cast<uint8_t*>(v_pool);
+  p.layer_offset = int64_t(layer) * num_kv_heads * capacity_tokens * head_dim;
+  p.capacity = capacity_tokens;
+  p.page_table = page_table;
+  p.page_table_stride = page_table_stride;
+  p.cache_lens = cache_lens;
+  p.batch = batch;
+  p.query_len = 1;
+  p.heads = num_kv_heads;
+  p.head_dim = head_dim;
+  p.page_shift = log2_int(page_size);
+  p.num_pages = int32_t(capacity_tokens / page_size);
+  p.error_word = error_word;
+  p.q_start = q_start;
+  p.token_request = token_request;
+  p.total_tokens = total_tokens;
+  cudaError_t err = hyt::run_kv_scatter(p, elem_bytes(dtype), static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "packed kv scatter launch");
+  return HYT_OK;
+}
+
+int hyt_norm_rope_scatter_packed(const void* q, const void* k, const void* v,
+                                 const int64_t* qkv_strides, const void* q_norm_weight,
+                                 const void* k_norm_weight, float eps, const float* cos,
+                                 const float* sin, int32_t rope_positions, void* q_out,
+                                 const int64_t* q_out_strides, void* k_pool, void* v_pool,
+                                 int32_t num_layers, int32_t layer, int64_t capacity_tokens,
+                                 const int32_t* page_table, int32_t page_table_stride,
+                                 const int32_t* cache_lens, const int32_t* q_start,
+                                 const int32_t* token_request, int32_t batch,
+                                 int32_t total_tokens, int32_t num_q_heads, int32_t num_kv_heads,
+                                 int32_t head_dim, int32_t page_size, int32_t dtype,
+                                 int32_t* error_word, void* stream) {
+  g_last_error.clear();
+  if (!q || !k || !v || !qkv_strides || !q_norm_weight || !k_norm_weight || !cos || !sin ||
+      !q_out || !q_out_strides || !k_pool || !v_pool || !page_table || !cache_lens || !q_start ||
+      !token_request)
+    return fail(HYT_ERR_INVALID, "null pointer argument");
+  if (total_tokens < 1) return fail(HYT_ERR_INVALID, "total_tokens must be positive");
+  Geometry g{num_layers, layer, capacity_tokens, page_table_stride, batch, 1,
+             num_q_heads, num_kv_heads, head_dim, page_size, dtype};
+  int rc = check_geometry(g);
+  if (rc != HYT_OK) return rc;
+  if (head_dim != 128) return fail(HYT_ERR_UNSUPPORTED, "fused norm/RoPE/scatter needs head_dim 128");
+  if (rope_positions < 1) return fail(HYT_ERR_INVALID, "rope_positions must be positive");
+  const int eb = elem_bytes(dtype);
+  const void* rows[4] = {q, k, v, q_out};
+  for (const void* r : rows)
+    if (reinterpret_cast<uintptr_t>(r) % (4 * eb)) return fail(HYT_ERR_INVALID, "q/k/v/q_out must be aligned to 4 elements");
+  for (int i = 0; i < 6; ++i)
+    if (qkv_strides[i] % 4) return fail(HYT_ERR_INVALID, "q/k/v strides must be multiples of 4 elements");
+  for (int i = 0; i < 2; ++i)
+    if (q_out_strides[i] % 4) return fail(HYT_ERR_INVALID, "q_out strides must be multiples of 4 elements");
+  if (reinterpret_cast<uintptr_t>(cos) % 16 || reinterpret_cast<uintptr_t>(sin) % 16)
+    return fail(HYT_ERR_INVALID, "cos/sin tables must be 16-byte aligned");
+  hyt::NormRopeParams p;
+  p.q = q;
+  p.q_sb = 0; p.q_st = qkv_strides[0]; p.q_sh = qkv_strides[1];
+  p.k = k;
+  p.k_sb = 0; p.k_st = qkv_strides[2]; p.k_sh = qkv_strides[3];
+  p.v = v;
+  p.v_sb = 0; p.v_st = qkv_strides[4]; p.v_sh = qkv_strides[5];
+  p.q_out = q_out;
+  p.o_sb = 0; p.o_st = q_out_strides[0]; p.o_sh = q_out_strides[1];
+  p.q_norm_weight = q_norm_weight;
+  p.k_norm_weight = k_norm_weight;
+  p.eps = eps;
+  p.cos = cos;
+  p.sin = sin;
+  p.rope_positions = rope_positions;
+  p.k_pool = k_pool;
+  p.v_pool = v_pool;
+  p.capacity = capacity_tokens;
+  p.layer = layer;
+  p.page_table = page_table;
+  p.page_table_stride = page_table_stride;
+  p.cache_lens = cache_lens;
+  p.batch = batch;
+  p.query_len = 1;
+  p.num_q_heads = num_q_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.page_shift = log2_int(page_size);
+  p.num_pages = int32_t(capacity_tokens / page_size);
+  p.error_word = error_word;
+  p.q_start = q_start;
+  p.token_request = token_request;
+  p.total_tokens = total_tokens;
+  cudaError_t err = hyt::run_norm_rope_scatter(p, dtype, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "packed norm/RoPE/scatter launch");
+  return HYT_OK;
+}
+
+int hyt_paged_attention_packed(const void* q, const int64_t* q_strides, const void* k_pool,
+                               const void* v_pool, int32_t num_layers, int32_t layer,
+                               int64_t capacity_tokens, const int32_t* page_table,
+                               int32_t page_table_stride, const int32_t* cache_lens,
+                               const int32_t* q_start, const int32_t* q_len, void* out,
+                               const int64_t* out_strides, int32_t batch, int32_t total_tokens,
+                               int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                               int32_t page_size, int32_t dtype, float scale,
+                               const int32_t* decode_ids, int32_t num_decode,
+                               const int32_t* prefill_ids, int32_t num_prefill,
+                               int32_t max_query_len, int32_t max_kv_len, int32_t split_tokens,
+                               void* workspace, size_t workspace_bytes, int32_t* error_word,
+                               void* stream) {
+  g_last_error.clear();
+  if (!q || !q_strides || !k_pool || !v_pool || !page_table || !cache_lens || !q_start ||
+      !q_len || !out || !out_strides)
+    return fail(HYT_ERR_INVALID, "null pointer argument");
+  if (num_decode < 0 || num_prefill < 0 || num_decode + num_prefill < 1)
+    return fail(HYT_ERR_INVALID, "the decode and prefill lists must hold at least one request");
+  if ((num_decode > 0 && !decode_ids) || (num_prefill > 0 && !prefill_ids))
+    return fail(HYT_ERR_INVALID, "null request list");
+  if (total_tokens < 1) return fail(HYT_ERR_INVALID, "total_tokens must be positive");
+  if (max_query_len < 1 || max_query_len > total_tokens)
+    return fail(HYT_ERR_INVALID, "max_query_len must be within [1, total_tokens]");
+  // b strides are unused for a packed batch: the kernels index rows by q_start
+  const int64_t qs[3] = {0, q_strides[1], q_strides[0]};
+  const int64_t os[3] = {0, out_strides[1], out_strides[0]};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = HYT_OK;
+  if (num_decode > 0) {
+    Geometry g{num_layers, layer, capacity_tokens, page_table_stride, batch, 1,
+               num_q_heads, num_kv_heads, head_dim, page_size, dtype};
+    rc = check_geometry(g);
+    if (rc != HYT_OK) return rc;
+    const PackedArgs pk{q_start, q_len, decode_ids, num_decode, total_tokens};
+    if (decode_eligible(g))
+      rc = launch_decode(q, qs, k_pool, v_pool, g, page_table, cache_lens, out, os, scale,
+                         max_kv_len, split_tokens, workspace, workspace_bytes, error_word, st, &pk);
+    else
+      rc = launch_generic(q, qs, k_pool, v_pool, g, page_table, cache_lens, out, os, scale,
+                          error_word, st, &pk);
+    if (rc != HYT_OK) return rc;
+  }
+  if (num_prefill > 0) {
+    Geometry g{num_layers, layer, capacity_tokens, page_table_stride, batch, max_query_len,
+               num_q_heads, num_kv_heads, head_dim, page_size, dtype};
+    rc = check_geometry(g);
+    if (rc != HYT_OK) return rc;
+    const PackedArgs pk{q_start, q_len, prefill_ids, num_prefill, total_tokens};
+    if (prefill_eligible(g, q, qs, out, os))
+      rc = launch_prefill(q, qs, k_pool, v_pool, g, page_table, cache_lens, out, os, scale,
+                          error_word, st, &pk);
+    else
+      rc = launch_generic(q, qs, k_pool, v_pool, g, page_table, cache_lens, out, os, scale,
+                          error_word, st, &pk);
+  }
+  return rc;
 }
 
 size_t hyt_attention_workspace_bytes(int32_t batch, int32_t query_len, int32_t num_q_heads,

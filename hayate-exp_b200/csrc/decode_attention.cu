@@ -21,6 +21,10 @@
 //     split writes its partial to the workspace and the last split to arrive
 //     (atomic counter, no waiting) merges all partials and resets the counter.
 //
+// Packed batches: a launch may serve a list of requests (AttentionParams::req_ids)
+// whose one-token chunks sit on a shared token axis; workspace slots follow the
+// launch index, so the workspace is sized for the list.
+//
 // Bytes per launch: sum_b kv_len[b] * H_kv * 128 * 2 (K and V) * elem_bytes,
 // which is what the roofline counts.
 #include <type_traits>
@@ -63,8 +67,14 @@ __global__ void __launch_bounds__(kThreads, 2)
                             const DecodeKernelParams P) {
   constexpr bool kHalf = std::is_same<T, __half>::value;
   const AttentionParams& p = P.a;
-  const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int split = blockIdx.x, g = blockIdx.y, z = blockIdx.z;
+  const int b = att_request(p, z);  // z == b unless the launch serves a request list
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // packed batches send only requests whose chunk has exactly query_len queries here
+  if (!att_request_ok(p, b) || att_query_len(p, b) != p.query_len) {
+    if (split == 0 && g == 0 && threadIdx.x == 0) flag_error(p.error_word, HYT_DEVERR_PACKED_RANGE);
+    return;
+  }
 
   const int cache_len = p.cache_lens[b];
   const int kv_len = cache_len + p.query_len;
@@ -145,13 +155,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     // Q rows: row r = local_head * query_len + t, zero past group * query_len.
     uint32_t qa[8][4];
     {
-      const T* qbase = static_cast<const T*>(p.q) + b * p.q_sb;
+      const T* qbase = static_cast<const T*>(p.q);
       const T* qrow[2] = {nullptr, nullptr};
       for (int half = 0; half < 2; ++half) {
         const int r = r0 + half * 8;
         if (r < P.rows) {
           const int hl = r / p.query_len, t = r - hl * p.query_len;
-          qrow[half] = qbase + int64_t(g * P.group + hl) * p.q_sh + int64_t(t) * p.q_st;
+          qrow[half] = qbase + att_q_row(p, b, t) + int64_t(g * P.group + hl) * p.q_sh;
         }
       }
 #pragma unroll
@@ -296,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   __syncthreads();
 
-  const int64_t unit = int64_t(b) * p.num_kv_heads + g;  // (request, kv head)
+  const int64_t unit = int64_t(z) * p.num_kv_heads + g;  // (launch request index, kv head)
   const int rows = P.rows;
   float* ws_o = P.d.ws_o + (unit * P.d.max_splits + split) * rows * kD;
   float* ws_ml = P.d.ws_ml + (unit * P.d.max_splits + split) * rows * 2;
@@ -315,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     if (nsplits == 1) {
       const int hl = r / p.query_len, t = r - hl * p.query_len;
-      T* out = static_cast<T*>(p.out) + b * p.o_sb + int64_t(g * P.group + hl) * p.o_sh + int64_t(t) * p.o_st;
+      T* out = static_cast<T*>(p.out) + att_o_row(p, b, t) + int64_t(g * P.group + hl) * p.o_sh;
       out[d] = Elem<T>::from_float(lsum > 0.f ? acc / lsum : 0.f);
     } else {
       ws_o[idx] = acc;
@@ -351,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       acc += __ldcg(&all_o[(int64_t(s) * rows + r) * kD + d]) * f;
     }
     const int hl = r / p.query_len, t = r - hl * p.query_len;
-    T* out = static_cast<T*>(p.out) + b * p.o_sb + int64_t(g * P.group + hl) * p.o_sh + int64_t(t) * p.o_st;
+    T* out = static_cast<T*>(p.out) + att_o_row(p, b, t) + int64_t(g * P.group + hl) * p.o_sh;
     out[d] = Elem<T>::from_float(lsum > 0.f ? acc / lsum : 0.f);
   }
   if (threadIdx.x == 0) P.d.ws_counter[unit] = 0;  // leave the counter zero for the next call
@@ -367,7 +377,7 @@ cudaError_t run_decode_attention(const AttentionParams& p, const DecodeLaunch& d
   P.d = d;
   P.group = p.num_q_heads / p.num_kv_heads;
   P.rows = P.group * p.query_len;
-  const dim3 grid(unsigned(d.max_splits), unsigned(p.num_kv_heads), unsigned(p.batch));
+  const dim3 grid(unsigned(d.max_splits), unsigned(p.num_kv_heads), unsigned(att_launch_count(p)));
   if (dtype == HYT_DTYPE_F16) {
     auto kernel = decode_attention_kernel<__half>;
     cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);

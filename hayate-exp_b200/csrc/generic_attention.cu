@@ -6,6 +6,9 @@
 // logical keys 0 .. cache_lens[b] + t, gathered through the page table; query
 // head h reads KV head h / (H_q / H_kv) (FlexAttention's enable_gqa mapping).
 //
+// Packed batches (per-request chunk lengths on one token axis) and request lists
+// (AttentionParams::req_ids) are served row by row the same way.
+//
 // One warp per query row; lane l holds dims l, l + 32, ... so every K/V row is
 // read by one coalesced warp access. Keys are taken four at a time so the four
 // warp reductions overlap. fp32 accumulation, base-2 online softmax.
@@ -21,17 +24,23 @@ template <typename T>
 __global__ void __launch_bounds__(kGenericWarps * 32) generic_attention_kernel(const AttentionParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = int64_t(blockIdx.x) * kGenericWarps + warp;
-  const int64_t rows = int64_t(p.batch) * p.num_q_heads * p.query_len;
+  const int64_t rows = int64_t(att_launch_count(p)) * p.num_q_heads * p.query_len;
   if (row >= rows) return;
   const int t = int(row % p.query_len);
   const int h = int((row / p.query_len) % p.num_q_heads);
-  const int b = int(row / (int64_t(p.query_len) * p.num_q_heads));
+  const int z = int(row / (int64_t(p.query_len) * p.num_q_heads));
+  const int b = att_request(p, z);
+  if (!att_request_ok(p, b)) {
+    if (t == 0 && h == 0 && lane == 0) flag_error(p.error_word, HYT_DEVERR_PACKED_RANGE);
+    return;
+  }
+  if (t >= att_query_len(p, b)) return;  // packed batch: past this request's chunk
   const int g = h / (p.num_q_heads / p.num_kv_heads);
   const int D = p.head_dim;
   const int n_keys = p.cache_lens[b] + t + 1;
   const int32_t page_mask = (1 << p.page_shift) - 1;
 
-  const T* q = static_cast<const T*>(p.q) + b * p.q_sb + h * p.q_sh + t * p.q_st;
+  const T* q = static_cast<const T*>(p.q) + att_q_row(p, b, t) + h * p.q_sh;
   const int64_t plane = (int64_t(p.layer) * p.num_kv_heads + g) * p.capacity;
   const T* kp = static_cast<const T*>(p.k_pool) + plane * D;
   const T* vp = static_cast<const T*>(p.v_pool) + plane * D;
@@ -96,7 +105,7 @@ __global__ void __launch_bounds__(kGenericWarps * 32) generic_attention_kernel(c
   }
   if (bad && lane == 0) flag_error(p.error_word, HYT_DEVERR_PAGE_RANGE);
   const float inv = l > 0.f ? 1.f / l : 0.f;
-  T* out = static_cast<T*>(p.out) + b * p.o_sb + h * p.o_sh + t * p.o_st;
+  T* out = static_cast<T*>(p.out) + att_o_row(p, b, t) + h * p.o_sh;
 #pragma unroll
   for (int e = 0; e < kGenericMaxPerLane; ++e) {
     const int d = lane + 32 * e;
@@ -105,7 +114,7 @@ __global__ void __launch_bounds__(kGenericWarps * 32) generic_attention_kernel(c
 }
 
 cudaError_t run_generic_attention(const AttentionParams& p, int dtype, cudaStream_t stream) {
-  const int64_t rows = int64_t(p.batch) * p.num_q_heads * p.query_len;
+  const int64_t rows = int64_t(att_launch_count(p)) * p.num_q_heads * p.query_len;
   const int64_t blocks = (rows + kGenericWarps - 1) / kGenericWarps;
   if (blocks <= 0) return cudaSuccess;
   if (blocks > INT32_MAX) return cudaErrorInvalidValue;

@@ -21,6 +21,12 @@ struct ScatterParams {
   const int32_t* cache_lens;
   int32_t batch, query_len, heads, head_dim, page_shift, num_pages;
   int32_t* error_word;
+  // Packed batch (token_request != nullptr): the new K/V rows of all requests share one
+  // token axis of total_tokens rows (strides k_st/v_st; k_sb/v_sb unused); token i
+  // belongs to request token_request[i] at position i - q_start[request] of its chunk.
+  const int32_t* q_start;
+  const int32_t* token_request;
+  int32_t total_tokens;
 };
 cudaError_t run_kv_scatter(const ScatterParams& p, int elem_bytes, cudaStream_t stream);
 
@@ -40,7 +46,50 @@ struct AttentionParams {
   int32_t batch, query_len, num_q_heads, num_kv_heads, head_dim, page_shift, num_pages;
   float scale;
   int32_t* error_word;
+  // Packed batch (q_start != nullptr): request b's queries are rows q_start[b] ..
+  // q_start[b] + q_len[b] - 1 of one token axis of total_tokens rows (strides q_st /
+  // o_st; q_sb / o_sb unused) and query_len is the longest q_len. req_ids, if set,
+  // lists the requests one launch serves (launch index z -> request req_ids[z], z <
+  // the launch's count); the other kernels of the same call serve the rest.
+  const int32_t* q_start;
+  const int32_t* q_len;
+  const int32_t* req_ids;
+  int32_t num_listed;  // entries of req_ids
+  int32_t total_tokens;
 };
+
+// Requests one launch serves (its grid's request dimension).
+__host__ __device__ inline int32_t att_launch_count(const AttentionParams& p) {
+  return p.req_ids != nullptr ? p.num_listed : p.batch;
+}
+
+#ifdef __CUDACC__
+// Request served by launch index z.
+__device__ __forceinline__ int att_request(const AttentionParams& p, int z) {
+  return p.req_ids != nullptr ? p.req_ids[z] : z;
+}
+// Queries of request b.
+__device__ __forceinline__ int att_query_len(const AttentionParams& p, int b) {
+  return p.q_start != nullptr ? p.q_len[b] : p.query_len;
+}
+// Element offset of query t of request b in q (head offset not included), and in out.
+__device__ __forceinline__ int64_t att_q_row(const AttentionParams& p, int b, int t) {
+  return p.q_start != nullptr ? (int64_t(p.q_start[b]) + t) * p.q_st
+                              : int64_t(b) * p.q_sb + int64_t(t) * p.q_st;
+}
+__device__ __forceinline__ int64_t att_o_row(const AttentionParams& p, int b, int t) {
+  return p.q_start != nullptr ? (int64_t(p.q_start[b]) + t) * p.o_st
+                              : int64_t(b) * p.o_sb + int64_t(t) * p.o_st;
+}
+// A packed request whose rows leave the token axis or exceed query_len, or a request id
+// outside the batch: refused (flagged, no work) so no q/out access leaves its tensor.
+__device__ __forceinline__ bool att_request_ok(const AttentionParams& p, int b) {
+  if (b < 0 || b >= p.batch) return false;
+  if (p.q_start == nullptr) return true;
+  const int s = p.q_start[b], n = p.q_len[b];
+  return s >= 0 && n >= 1 && n <= p.query_len && int64_t(s) + n <= p.total_tokens;
+}
+#endif
 
 // CUDA-core path: any dtype (0 bf16, 1 f16, 2 f32), head_dim % 8 == 0, <= 256.
 cudaError_t run_generic_attention(const AttentionParams& p, int dtype, cudaStream_t stream);
@@ -88,6 +137,11 @@ struct NormRopeParams {
   const int32_t* cache_lens;
   int32_t batch, query_len, num_q_heads, num_kv_heads, page_shift, num_pages;
   int32_t* error_word;
+  // Packed batch, as in ScatterParams: q/k/v/q_out rows on one token axis of
+  // total_tokens rows (b strides unused), token i of request token_request[i].
+  const int32_t* q_start;
+  const int32_t* token_request;
+  int32_t total_tokens;
 };
 cudaError_t run_norm_rope_scatter(const NormRopeParams& p, int dtype, cudaStream_t stream);
 

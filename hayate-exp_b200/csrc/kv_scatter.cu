@@ -6,6 +6,9 @@
 // page_table[b][pos / P] * P + pos % P of pool[layer, 0, h]. The copy is a byte
 // move (bit-exact with the reference's index_put).
 //
+// Packed batches (chunks of different lengths on one token axis, token_request set)
+// take the same copy with each token's request and position looked up per token.
+//
 // Layout: consecutive threads take consecutive VEC-byte chunks of one row, so a
 // warp moves whole 256-byte rows of a bf16 head_dim-128 vector with coalesced
 // 16-byte loads and stores. HBM-bound; the work per launch is tiny at decode
@@ -26,7 +29,8 @@ __global__ void __launch_bounds__(256) kv_scatter_kernel(const ScatterParams p) 
                                                           uint16_t>::type>::type>::type;
   constexpr int kVecElems = kVecBytes / kElemBytes;
   const int chunks = p.head_dim / kVecElems;
-  const int64_t rows = int64_t(p.batch) * p.query_len * p.heads;
+  const bool packed = p.token_request != nullptr;
+  const int64_t rows = (packed ? int64_t(p.total_tokens) : int64_t(p.batch) * p.query_len) * p.heads;
   const int64_t total = 2 * rows * chunks;
   const int32_t page_mask = (1 << p.page_shift) - 1;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total;
@@ -36,8 +40,26 @@ __global__ void __launch_bounds__(256) kv_scatter_kernel(const ScatterParams p) 
     const bool is_v = row >= rows;
     if (is_v) row -= rows;
     const int h = int(row % p.heads);
-    const int t = int((row / p.heads) % p.query_len);
-    const int b = int(row / (int64_t(p.heads) * p.query_len));
+    int t, b;
+    int64_t token_elem;  // element offset of this token's row (head offset not included)
+    if (packed) {
+      const int64_t tok = row / p.heads;
+      b = p.token_request[tok];
+      if (b < 0 || b >= p.batch) {
+        flag_error(p.error_word, HYT_DEVERR_PACKED_RANGE);
+        continue;
+      }
+      t = int(tok - p.q_start[b]);
+      if (t < 0) {
+        flag_error(p.error_word, HYT_DEVERR_PACKED_RANGE);
+        continue;
+      }
+      token_elem = tok * (is_v ? p.v_st : p.k_st);
+    } else {
+      t = int((row / p.heads) % p.query_len);
+      b = int(row / (int64_t(p.heads) * p.query_len));
+      token_elem = is_v ? (b * p.v_sb + t * p.v_st) : (b * p.k_sb + t * p.k_st);
+    }
     const int64_t pos = int64_t(p.cache_lens[b]) + t;
     const int64_t logical_page = pos >> p.page_shift;
     if (pos < 0 || logical_page >= p.page_table_stride) {
@@ -50,8 +72,7 @@ __global__ void __launch_bounds__(256) kv_scatter_kernel(const ScatterParams p) 
       continue;
     }
     const int64_t slot = (int64_t(page) << p.page_shift) + (pos & page_mask);
-    const int64_t src_elem = is_v ? (b * p.v_sb + h * p.v_sh + t * p.v_st)
-                                  : (b * p.k_sb + h * p.k_sh + t * p.k_st);
+    const int64_t src_elem = token_elem + h * (is_v ? p.v_sh : p.k_sh);
     const int64_t dst_elem = p.layer_offset + (h * p.capacity + slot) * p.head_dim;
     const uint8_t* src = (is_v ? p.v_new : p.k_new) + (src_elem + int64_t(chunk) * kVecElems) * kElemBytes;
     uint8_t* dst = (is_v ? p.v_pool : p.k_pool) + (dst_elem + int64_t(chunk) * kVecElems) * kElemBytes;
@@ -62,7 +83,8 @@ __global__ void __launch_bounds__(256) kv_scatter_kernel(const ScatterParams p) 
 template <int kElemBytes, int kVecBytes>
 static cudaError_t launch_scatter(const ScatterParams& p, cudaStream_t stream) {
   constexpr int kVecElems = kVecBytes / kElemBytes;
-  const int64_t total = 2ll * p.batch * p.query_len * p.heads * (p.head_dim / kVecElems);
+  const int64_t tokens = p.token_request != nullptr ? int64_t(p.total_tokens) : int64_t(p.batch) * p.query_len;
+  const int64_t total = 2 * tokens * p.heads * (p.head_dim / kVecElems);
   const int threads = 256;
   int64_t blocks = (total + threads - 1) / threads;
   if (blocks > 148 * 16) blocks = 148 * 16;  // grid-stride beyond 16 blocks per SM

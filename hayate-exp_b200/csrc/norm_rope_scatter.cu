@@ -13,6 +13,8 @@
 // fp32 products of that rounded value with the fp32 tables (separate multiply and add,
 // as torch evaluates them) and is rounded once more.
 //
+// Packed batches (token_request set) look each token's request and position up.
+//
 // One warp per (token, head row); each lane holds 4 consecutive features, so the
 // rotation partner (feature i +/- 64) sits in lane ^ 16. HBM-bound: every byte of
 // q, k, v is read once and written once.
@@ -55,11 +57,29 @@ template <typename T>
 __global__ void __launch_bounds__(kWarps * 32) norm_rope_scatter_kernel(const NormRopeParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int heads = p.num_q_heads + 2 * p.num_kv_heads;
+  const bool packed = p.token_request != nullptr;
+  const int64_t tokens = packed ? int64_t(p.total_tokens) : int64_t(p.batch) * p.query_len;
   const int64_t row = int64_t(blockIdx.x) * kWarps + warp;
-  if (row >= int64_t(p.batch) * p.query_len * heads) return;
+  if (row >= tokens * heads) return;
   const int which = int(row % heads);
   const int64_t token = row / heads;
-  const int t = int(token % p.query_len), b = int(token / p.query_len);
+  int t, b;
+  if (packed) {
+    b = p.token_request[token];
+    t = (b >= 0 && b < p.batch) ? int(token - p.q_start[b]) : -1;
+    if (t < 0) {
+      flag_error(p.error_word, HYT_DEVERR_PACKED_RANGE);
+      return;
+    }
+  } else {
+    t = int(token % p.query_len);
+    b = int(token / p.query_len);
+  }
+  // element offsets of this token in q/k/v ({b, t} part) and in q_out
+  const int64_t q_tok = packed ? token * p.q_st : b * p.q_sb + t * p.q_st;
+  const int64_t k_tok = packed ? token * p.k_st : b * p.k_sb + t * p.k_st;
+  const int64_t v_tok = packed ? token * p.v_st : b * p.v_sb + t * p.v_st;
+  const int64_t o_tok = packed ? token * p.o_st : b * p.o_sb + t * p.o_st;
   const int pos = p.cache_lens[b] + t;
   const int d0 = lane * 4;  // this lane's features d0 .. d0 + 3 (head_dim 128)
 
@@ -68,13 +88,13 @@ __global__ void __launch_bounds__(kWarps * 32) norm_rope_scatter_kernel(const No
   int h;
   if (which < p.num_q_heads) {
     kind = 0, h = which;
-    src = static_cast<const T*>(p.q) + b * p.q_sb + t * p.q_st + int64_t(h) * p.q_sh;
+    src = static_cast<const T*>(p.q) + q_tok + int64_t(h) * p.q_sh;
   } else if (which < p.num_q_heads + p.num_kv_heads) {
     kind = 1, h = which - p.num_q_heads;
-    src = static_cast<const T*>(p.k) + b * p.k_sb + t * p.k_st + int64_t(h) * p.k_sh;
+    src = static_cast<const T*>(p.k) + k_tok + int64_t(h) * p.k_sh;
   } else {
     kind = 2, h = which - p.num_q_heads - p.num_kv_heads;
-    src = static_cast<const T*>(p.v) + b * p.v_sb + t * p.v_st + int64_t(h) * p.v_sh;
+    src = static_cast<const T*>(p.v) + v_tok + int64_t(h) * p.v_sh;
   }
   float x[4];
   load4<T>(src + d0, x);
@@ -111,7 +131,7 @@ __global__ void __launch_bounds__(kWarps * 32) norm_rope_scatter_kernel(const No
   }
 
   if (kind == 0) {
-    T* dst = static_cast<T*>(p.q_out) + b * p.o_sb + int64_t(h) * p.o_sh + t * p.o_st;
+    T* dst = static_cast<T*>(p.q_out) + o_tok + int64_t(h) * p.o_sh;
     store4<T>(dst + d0, x);
     return;
   }
@@ -135,7 +155,8 @@ __global__ void __launch_bounds__(kWarps * 32) norm_rope_scatter_kernel(const No
 }  // namespace
 
 cudaError_t run_norm_rope_scatter(const NormRopeParams& p, int dtype, cudaStream_t stream) {
-  const int64_t rows = int64_t(p.batch) * p.query_len * (p.num_q_heads + 2 * p.num_kv_heads);
+  const int64_t tokens = p.token_request != nullptr ? int64_t(p.total_tokens) : int64_t(p.batch) * p.query_len;
+  const int64_t rows = tokens * (p.num_q_heads + 2 * p.num_kv_heads);
   const int64_t blocks = (rows + kWarps - 1) / kWarps;
   if (blocks <= 0) return cudaSuccess;
   if (blocks > INT32_MAX) return cudaErrorInvalidValue;

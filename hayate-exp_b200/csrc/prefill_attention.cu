@@ -38,6 +38,10 @@
 // TMEM (512 columns): S_A/P_A [0,128), S_B/P_B [128,256), O_A [256,384), O_B [384,512).
 // Shared memory: Q_A, Q_B 32 KB each, K and V 2 x 32 KB each (192 KB), 6 KB exchange.
 //
+// Packed batches (AttentionParams::q_start) give each request its own chunk length on a
+// shared token axis; query tiles past a request's chunk exit at once, and a request
+// list (req_ids) picks the requests the launch serves.
+//
 // FLOPs per launch counted by the roofline: 4 * H_q * 128 per causal-valid
 // (query, key) pair.
 #include <type_traits>
@@ -122,7 +126,7 @@ struct Barriers {
 static_assert(sizeof(Barriers) <= 256, "barrier block");
 
 // 96 registers: 18 warps over 4 sub-partitions put 5 warps on one 16K-register file.
-template <typename T>
+template <typename T, bool kPacked>
 __global__ void __maxnreg__(96)
     prefill_attention_kernel(const __grid_constant__ CUtensorMap k_map,
                              const __grid_constant__ CUtensorMap v_map,
@@ -131,7 +135,7 @@ __global__ void __maxnreg__(96)
   const AttentionParams& p = P.a;
   // heavier (later) query tiles first: they see the most keys
   const int q_tile = int(gridDim.x) - 1 - int(blockIdx.x);
-  const int pair = blockIdx.y, b = blockIdx.z;
+  const int pair = blockIdx.y, b = kPacked ? att_request(p, blockIdx.z) : int(blockIdx.z);
   const int h0 = pair * 2;  // tiles A and B: heads h0 and h0 + 1 of KV group g
   const int g = h0 / P.group;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -140,9 +144,24 @@ __global__ void __maxnreg__(96)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Barriers* bars = reinterpret_cast<Barriers*>(smem + kBarOff);
 
-  const int cache_len = p.cache_lens[b];
+  // packed batches: this request's chunk length; tiles past it have no work (uniform
+  // per CTA, decided before any barrier or TMEM allocation)
+  if (kPacked && !att_request_ok(p, b)) {
+    if (q_tile == 0 && pair == 0 && threadIdx.x == 0) flag_error(p.error_word, HYT_DEVERR_PACKED_RANGE);
+    return;
+  }
+  const int query_len = kPacked ? p.q_len[b] : p.query_len;
+  // element offsets of query row t of this request in q and in out (head offset apart)
+  auto q_row = [&](int t) -> int64_t {
+    return kPacked ? (int64_t(p.q_start[b]) + t) * p.q_st : int64_t(b) * p.q_sb + int64_t(t) * p.q_st;
+  };
+  auto o_row = [&](int t) -> int64_t {
+    return kPacked ? (int64_t(p.q_start[b]) + t) * p.o_st : int64_t(b) * p.o_sb + int64_t(t) * p.o_st;
+  };
   const int t0 = q_tile * kRows;
-  const int t_last = min(t0 + kRows, p.query_len) - 1;
+  if (t0 >= query_len) return;
+  const int cache_len = p.cache_lens[b];
+  const int t_last = min(t0 + kRows, query_len) - 1;
   const int n_tiles = (cache_len + t_last) / kKeys + 1;
   const int32_t* table = p.page_table + int64_t(b) * p.page_table_stride;
   const int page_mask = (1 << p.page_shift) - 1;
@@ -165,8 +184,8 @@ __global__ void __maxnreg__(96)
     if (threadIdx.x == 0) flag_error(p.error_word, bad);
     for (int idx = threadIdx.x; idx < 2 * kRows * kD; idx += kThreads) {
       const int x = idx / (kRows * kD), r = (idx / kD) % kRows, d = idx % kD;
-      if (t0 + r < p.query_len) {
-        T* out = static_cast<T*>(p.out) + b * p.o_sb + int64_t(h0 + x) * p.o_sh + int64_t(t0 + r) * p.o_st;
+      if (t0 + r < query_len) {
+        T* out = static_cast<T*>(p.out) + o_row(t0 + r) + int64_t(h0 + x) * p.o_sh;
         out[d] = Elem<T>::from_float(0.f);
       }
     }
@@ -328,8 +347,8 @@ __global__ void __maxnreg__(96)
     const int x = warp >> 3, half = (warp >> 2) & 1, quarter = warp & 3;
     const int r = quarter * 32 + lane;  // query row == TMEM lane
     const int t = t0 + r;
-    const bool row_valid = t < p.query_len;
-    const int limit = cache_len + min(t, p.query_len - 1);  // last visible key
+    const bool row_valid = t < query_len;
+    const int limit = cache_len + min(t, query_len - 1);  // last visible key
     const uint32_t lane_addr = tmem + (uint32_t(quarter * 32) << 16);
     const int pair_bar = 1 + x * 4 + quarter;  // named barrier of the two warps of this row quarter
     float* red_max = reinterpret_cast<float*>(smem + kRedOff) + x * (2 * 2 * kRows);  // [parity][half][row]
@@ -338,12 +357,12 @@ __global__ void __maxnreg__(96)
     {  // Q rows -> swizzled shared memory: two threads per row, 8 chunks each
       const int qx = threadIdx.x >> 8, qr = (threadIdx.x >> 1) & 127, qc = (threadIdx.x & 1) * 8;
       const int qt = t0 + qr;
-      const T* qrow = static_cast<const T*>(p.q) + b * p.q_sb + int64_t(h0 + qx) * p.q_sh + int64_t(qt) * p.q_st;
+      const T* qrow = static_cast<const T*>(p.q) + q_row(qt) + int64_t(h0 + qx) * p.q_sh;
       uint8_t* qdst = smem + kQOff + qx * kTileBytes;
 #pragma unroll
       for (int c = qc; c < qc + 8; ++c) {
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (qt < p.query_len) v = reinterpret_cast<const uint4*>(qrow)[c];
+        if (qt < query_len) v = reinterpret_cast<const uint4*>(qrow)[c];
         *reinterpret_cast<uint4*>(qdst + sw128_offset(qr, c)) = v;
       }
       fence_proxy_async_smem();
@@ -419,7 +438,7 @@ __global__ void __maxnreg__(96)
     named_bar_sync(pair_bar, 64);
     const float l = red_sum[r] + red_sum[kRows + r];
     const float inv = l > 0.f ? 1.f / l : 0.f;
-    T* out = static_cast<T*>(p.out) + b * p.o_sb + int64_t(h0 + x) * p.o_sh + int64_t(t) * p.o_st + half * 64;
+    T* out = static_cast<T*>(p.out) + o_row(t) + int64_t(h0 + x) * p.o_sh + half * 64;
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       uint32_t o[32];
@@ -456,18 +475,21 @@ cudaError_t run_prefill_attention(const AttentionParams& p, const CUtensorMap& k
   P.a = p;
   P.group = p.num_q_heads / p.num_kv_heads;
   const dim3 grid(unsigned((p.query_len + kRows - 1) / kRows), unsigned(p.num_q_heads / 2),
-                  unsigned(p.batch));
-  if (dtype == HYT_DTYPE_F16) {
-    auto kernel = prefill_attention_kernel<__half>;
+                  unsigned(att_launch_count(p)));
+  auto launch = [&](auto kernel) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
     kernel<<<grid, kThreads, kSmemBytes, stream>>>(k_map, v_map, P);
-  } else {
-    auto kernel = prefill_attention_kernel<__nv_bfloat16>;
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    kernel<<<grid, kThreads, kSmemBytes, stream>>>(k_map, v_map, P);
-  }
+    return cudaSuccess;
+  };
+  const bool packed = p.q_start != nullptr;
+  cudaError_t e;
+  if (dtype == HYT_DTYPE_F16)
+    e = packed ? launch(prefill_attention_kernel<__half, true>) : launch(prefill_attention_kernel<__half, false>);
+  else
+    e = packed ? launch(prefill_attention_kernel<__nv_bfloat16, true>)
+               : launch(prefill_attention_kernel<__nv_bfloat16, false>);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -20,6 +20,7 @@ DEVICE_ERRORS = {
     4: "kv length beyond the max_kv_len the launch was sized for",
     8: "a bounded pipeline wait gave up",
     16: "tensor-core ops issued on other than exactly one lane (work skipped)",
+    32: "packed batch metadata (q_start / q_len / request id) out of range",
 }
 
 _c_i32, _c_i64, _c_f32, _c_size, _c_p = (ctypes.c_int32, ctypes.c_int64, ctypes.c_float,
@@ -43,6 +44,20 @@ SIGNATURES = {
                                              _c_i32, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i64,
                                              _c_p, _c_i32, _c_p, _c_i32, _c_i32, _c_i32, _c_i32,
                                              _c_i32, _c_i32, _c_i32, _c_p, _c_p]),
+    # packed (mixed prefill + decode) batches
+    "hyt_kv_scatter_packed": (ctypes.c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i64,
+                                             _c_p, _c_i32, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32,
+                                             _c_i32, _c_i32, _c_i32, _c_p, _c_p]),
+    "hyt_norm_rope_scatter_packed": (ctypes.c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_f32, _c_p,
+                                                    _c_p, _c_i32, _c_p, _c_p, _c_p, _c_p, _c_i32,
+                                                    _c_i32, _c_i64, _c_p, _c_i32, _c_p, _c_p, _c_p,
+                                                    _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
+                                                    _c_i32, _c_p, _c_p]),
+    "hyt_paged_attention_packed": (ctypes.c_int, [_c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i64, _c_p,
+                                                  _c_i32, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32,
+                                                  _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_f32, _c_p,
+                                                  _c_i32, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_p,
+                                                  _c_size, _c_p, _c_p]),
     "hyt_attention_workspace_bytes": (_c_size, [_c_i32] * 8),
     "hyt_workspace_init": (ctypes.c_int, [_c_p, _c_size, _c_p]),
 }

@@ -196,6 +196,132 @@ def paged_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
     return out
 
 
+# ---------------------------------------------------------------------------- packed batches
+def _th_strides(t: torch.Tensor, name: str) -> tuple[int, int]:
+    """Element strides {token, head} of a ``[1, H, N, D]`` packed tensor."""
+    if t.dim() != 4 or t.shape[0] != 1:
+        raise ValueError(f"{name} must be [1, heads, total_tokens, head_dim]")
+    if t.stride(3) != 1 and t.size(3) > 1:
+        raise ValueError(f"{name} must have a contiguous last dimension")
+    return t.stride(2), t.stride(1)
+
+
+def _int32_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t.dtype != torch.int32 or not t.is_contiguous():
+            raise TypeError("packed-batch metadata must be contiguous int32 tensors")
+
+
+def kv_scatter_packed(k_new: torch.Tensor, v_new: torch.Tensor, k_pool: torch.Tensor,
+                      v_pool: torch.Tensor, layer: int, page_table: torch.Tensor,
+                      cache_lens: torch.Tensor, q_start: torch.Tensor, token_request: torch.Tensor,
+                      page_size: int, error_word: torch.Tensor | None = None) -> None:
+    """Kernel (a) on a packed batch: ``[1, H_kv, N, D]`` new K/V, token i of request
+    ``token_request[i]`` at position ``cache_lens[b] + i - q_start[b]``."""
+    _require_cuda(k_new, v_new, k_pool, v_pool, page_table, cache_lens, q_start, token_request)
+    _int32_cuda(q_start, token_request)
+    num_layers, heads, capacity, head_dim = _pool_geometry(k_pool, v_pool)
+    if k_new.shape != v_new.shape or k_new.dtype != k_pool.dtype or v_new.dtype != k_pool.dtype:
+        raise ValueError("k/v must share one shape and the pool dtype")
+    _, h, total, d = k_new.shape
+    if h != heads or d != head_dim or token_request.numel() != total:
+        raise ValueError("k/v heads, head_dim and token count must match the pool and metadata")
+    batch = cache_lens.numel()
+    strides = _lib.int64_array(_th_strides(k_new, "k") + _th_strides(v_new, "v"))
+    pts = _table_args(page_table, cache_lens, batch)
+    rc = _lib.lib().hyt_kv_scatter_packed(
+        k_new.data_ptr(), v_new.data_ptr(), strides, k_pool.data_ptr(), v_pool.data_ptr(),
+        num_layers, layer, capacity, page_table.data_ptr(), pts, cache_lens.data_ptr(),
+        q_start.data_ptr(), token_request.data_ptr(), batch, total, heads, head_dim, page_size,
+        dtype_code(k_pool.dtype), _ptr(error_word), _stream_ptr())
+    _lib.check(rc, "hyt_kv_scatter_packed")
+
+
+def norm_rope_scatter_packed(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                             q_norm_weight: torch.Tensor, k_norm_weight: torch.Tensor,
+                             cos: torch.Tensor, sin: torch.Tensor, k_pool: torch.Tensor,
+                             v_pool: torch.Tensor, layer: int, page_table: torch.Tensor,
+                             cache_lens: torch.Tensor, q_start: torch.Tensor,
+                             token_request: torch.Tensor, page_size: int, eps: float = 1e-6,
+                             error_word: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused QK-norm + RoPE + scatter on a packed batch: q/k/v are the projections as
+    ``[1, N, H, 128]``; returns the rotated q as ``[1, H_q, N, 128]`` (backed by
+    ``[1, N, H_q, 128]`` memory)."""
+    _require_cuda(q, k, v, q_norm_weight, k_norm_weight, cos, sin, k_pool, v_pool, page_table,
+                  cache_lens, q_start, token_request)
+    _int32_cuda(q_start, token_request)
+    num_layers, num_kv_heads, capacity, head_dim = _pool_geometry(k_pool, v_pool)
+    if q.dim() != 4 or q.shape[0] != 1 or k.shape != v.shape or k.shape[:2] != q.shape[:2]:
+        raise ValueError("q, k, v must be [1, total_tokens, heads, head_dim]")
+    _, total, num_q_heads, d = q.shape
+    if d != head_dim or k.shape[2] != num_kv_heads or token_request.numel() != total:
+        raise ValueError("q/k/v shapes do not match the pools and metadata")
+    for t in (q, k, v, q_norm_weight, k_norm_weight):
+        if t.dtype != k_pool.dtype:
+            raise ValueError("q/k/v and the norm weights must have the pool dtype")
+    if cos.dtype != torch.float32 or sin.dtype != torch.float32 or not (cos.is_contiguous() and sin.is_contiguous()):
+        raise ValueError("cos/sin must be contiguous fp32 [positions, head_dim] tables")
+    for t, name in ((q, "q"), (k, "k"), (v, "v")):
+        if t.stride(3) != 1:
+            raise ValueError(f"{name} must have a contiguous last dimension")
+    q_out = torch.empty((1, total, num_q_heads, head_dim), dtype=q.dtype, device=q.device).transpose(1, 2)
+    strides = _lib.int64_array([q.stride(1), q.stride(2), k.stride(1), k.stride(2), v.stride(1), v.stride(2)])
+    out_strides = _lib.int64_array(_th_strides(q_out, "q_out"))
+    batch = cache_lens.numel()
+    pts = _table_args(page_table, cache_lens, batch)
+    rc = _lib.lib().hyt_norm_rope_scatter_packed(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), strides, q_norm_weight.data_ptr(),
+        k_norm_weight.data_ptr(), float(eps), cos.data_ptr(), sin.data_ptr(), cos.shape[0],
+        q_out.data_ptr(), out_strides, k_pool.data_ptr(), v_pool.data_ptr(), num_layers, layer,
+        capacity, page_table.data_ptr(), pts, cache_lens.data_ptr(), q_start.data_ptr(),
+        token_request.data_ptr(), batch, total, num_q_heads, num_kv_heads, head_dim, page_size,
+        dtype_code(q.dtype), _ptr(error_word), _stream_ptr())
+    _lib.check(rc, "hyt_norm_rope_scatter_packed")
+    return q_out
+
+
+def paged_attention_packed(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, layer: int,
+                           page_table: torch.Tensor, cache_lens: torch.Tensor, q_start: torch.Tensor,
+                           q_len: torch.Tensor, decode_ids: torch.Tensor, prefill_ids: torch.Tensor,
+                           page_size: int, max_query_len: int, max_kv_len: int,
+                           scale: float | None = None, out: torch.Tensor | None = None,
+                           workspace: torch.Tensor | None = None,
+                           error_word: torch.Tensor | None = None, split_tokens: int = 0) -> torch.Tensor:
+    """Causal GQA attention of a packed batch ``q`` ``[1, H_q, N, D]``: the requests in
+    ``decode_ids`` (one query each) on the decode kernel, those in ``prefill_ids`` on the
+    prefill kernel, in one call."""
+    _require_cuda(q, k_pool, v_pool, page_table, cache_lens, q_start, q_len, decode_ids, prefill_ids)
+    _int32_cuda(q_start, q_len, decode_ids, prefill_ids)
+    num_layers, num_kv_heads, capacity, head_dim = _pool_geometry(k_pool, v_pool)
+    _, num_q_heads, total, d = q.shape
+    if d != head_dim or q.dtype != k_pool.dtype:
+        raise ValueError("q must match the pool's head_dim and dtype")
+    if out is None:
+        out = torch.empty((1, total, num_q_heads, head_dim), dtype=q.dtype, device=q.device).transpose(1, 2)
+    if out.shape != q.shape or out.dtype != q.dtype:
+        raise ValueError("out must match q")
+    qs = _lib.int64_array(_th_strides(q, "q"))
+    os_ = _lib.int64_array(_th_strides(out, "out"))
+    batch = cache_lens.numel()
+    pts = _table_args(page_table, cache_lens, batch)
+    n_dec, n_pre = decode_ids.numel(), prefill_ids.numel()
+    scale = 1.0 / math.sqrt(head_dim) if scale is None else float(scale)
+    need = attention_workspace_bytes(n_dec, 1, num_q_heads, num_kv_heads, head_dim, max_kv_len,
+                                     q.dtype, split_tokens) if n_dec else 0
+    if need and (workspace is None or workspace.numel() < need):
+        raise RuntimeError(f"attention needs a zeroed workspace of {need} bytes")
+    rc = _lib.lib().hyt_paged_attention_packed(
+        q.data_ptr(), qs, k_pool.data_ptr(), v_pool.data_ptr(), num_layers, layer, capacity,
+        page_table.data_ptr(), pts, cache_lens.data_ptr(), q_start.data_ptr(), q_len.data_ptr(),
+        out.data_ptr(), os_, batch, total, num_q_heads, num_kv_heads, head_dim, page_size,
+        dtype_code(q.dtype), scale, decode_ids.data_ptr() if n_dec else None, n_dec,
+        prefill_ids.data_ptr() if n_pre else None, n_pre, max_query_len, max_kv_len, split_tokens,
+        _ptr(workspace) if need else None, workspace.numel() if need else 0, _ptr(error_word),
+        _stream_ptr())
+    _lib.check(rc, "hyt_paged_attention_packed")
+    return out
+
+
 def read_device_errors(error_word: torch.Tensor) -> list[str]:
     """Decode (and synchronise on) a device error word; empty if no kernel refused anything."""
     value = int(error_word.item())

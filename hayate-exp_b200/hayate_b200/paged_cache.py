@@ -162,13 +162,32 @@ class _SlotPageTable:
         return self.dev[:, :width].index_select(0, slots)
 
 
+@dataclass
+class PackedLayout:
+    """Where each request's new tokens sit on a packed batch's shared token axis."""
+
+    query_lens: list[int]      # tokens of each request this step
+    total_tokens: int
+    q_start: torch.Tensor      # [B] int32: first token row of each request
+    q_len: torch.Tensor        # [B] int32
+    token_request: torch.Tensor  # [total_tokens] int32: request of each token row
+    decode_ids: torch.Tensor   # requests with one token (split-KV decode kernel)
+    prefill_ids: torch.Tensor  # the others (tcgen05 prefill kernel)
+
+
 class PagedKVBatch:
-    """Per-step metadata shared by every layer of one forward pass."""
+    """Per-step metadata shared by every layer of one forward pass.
+
+    A packed batch (``begin_batch`` given one query length per request) puts every
+    request's new tokens on one token axis, in batch order: tensors are ``[1, H, N, D]``
+    (``N`` = total new tokens) and ``layout`` says which rows belong to which request.
+    """
 
     __slots__ = ("k_cache", "v_cache", "page_table", "cache_lens", "page_size", "query_len",
-                 "max_kv_len", "cache_lens_i32", "_manager", "_meta")
+                 "max_kv_len", "cache_lens_i32", "layout", "_manager", "_meta")
 
-    def __init__(self, manager, page_table, cache_lens, cache_lens_i32, query_len, max_kv_len, meta):
+    def __init__(self, manager, page_table, cache_lens, cache_lens_i32, query_len, max_kv_len, meta,
+                 layout: PackedLayout | None = None):
         self.k_cache = manager.k_cache
         self.v_cache = manager.v_cache
         self.page_table = page_table
@@ -177,11 +196,15 @@ class PagedKVBatch:
         self.page_size = manager.page_size
         self.query_len = query_len
         self.max_kv_len = max_kv_len
+        self.layout = layout
         self._manager = manager
         self._meta = meta  # keeps the uploaded buffer alive while kernels read it
 
     def write_layer(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor) -> None:
         """Scatter the step's new K/V ``[B, H_kv, T, D]`` into this layer's pages."""
+        if self.layout is not None:
+            self._write_packed(layer_idx, k, v)
+            return
         if k.shape[2] != self.query_len or v.shape != k.shape:
             raise ValueError("k and v must be [batch, kv_heads, query_len, head_dim]")
         if k.stride(-1) != 1:
@@ -201,6 +224,14 @@ class PagedKVBatch:
         unfused path (norm -> transpose -> RoPE -> ``write_layer``) writes. Returns the
         rotated ``q`` as ``[B, H_q, T, D]``, ready for ``attend_layer``.
         """
+        if self.layout is not None:
+            lay = self.layout
+            if q.shape[0] != 1 or q.shape[1] != lay.total_tokens:
+                raise ValueError("a packed batch's q/k/v are [1, total_tokens, heads, head_dim]")
+            return ops.norm_rope_scatter_packed(
+                q, k, v, q_norm_weight, k_norm_weight, cos, sin, self.k_cache, self.v_cache,
+                layer_idx, self.page_table, self.cache_lens_i32, lay.q_start, lay.token_request,
+                self.page_size, eps=eps, error_word=self._manager.error_word)
         if q.shape[1] != self.query_len:
             raise ValueError("q/k/v must carry query_len tokens")
         return ops.norm_rope_scatter(q, k, v, q_norm_weight, k_norm_weight, cos, sin, self.k_cache,
@@ -212,11 +243,34 @@ class PagedKVBatch:
         if q.stride(-1) != 1:
             q = q.contiguous()
         manager = self._manager
+        if self.layout is not None:
+            lay = self.layout
+            if q.shape[0] != 1 or q.shape[2] != lay.total_tokens:
+                raise ValueError("a packed batch's q is [1, H_q, total_tokens, head_dim]")
+            n_dec = lay.decode_ids.numel()
+            workspace = manager.workspace_for(n_dec, 1, q.shape[1], self.max_kv_len) if n_dec else None
+            return ops.paged_attention_packed(
+                q, self.k_cache, self.v_cache, layer_idx, self.page_table, self.cache_lens_i32,
+                lay.q_start, lay.q_len, lay.decode_ids, lay.prefill_ids, self.page_size,
+                self.query_len, self.max_kv_len, workspace=workspace, error_word=manager.error_word,
+                split_tokens=manager.split_tokens)
         workspace = manager.workspace_for(q.shape[0], self.query_len, q.shape[1], self.max_kv_len)
         return ops.paged_attention(q, self.k_cache, self.v_cache, layer_idx, self.page_table,
                                    self.cache_lens_i32, self.page_size, self.max_kv_len,
                                    workspace=workspace, error_word=manager.error_word,
                                    kernel=manager.kernel, split_tokens=manager.split_tokens)
+
+    def _write_packed(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor) -> None:
+        lay = self.layout
+        if k.shape[0] != 1 or k.shape[2] != lay.total_tokens or v.shape != k.shape:
+            raise ValueError("a packed batch's k and v are [1, kv_heads, total_tokens, head_dim]")
+        if k.stride(-1) != 1:
+            k = k.contiguous()
+        if v.stride(-1) != 1:
+            v = v.contiguous()
+        ops.kv_scatter_packed(k, v, self.k_cache, self.v_cache, layer_idx, self.page_table,
+                              self.cache_lens_i32, lay.q_start, lay.token_request, self.page_size,
+                              error_word=self._manager.error_word)
 
 
 class PagedKVCacheManager:
@@ -395,11 +449,24 @@ class PagedKVCacheManager:
         self._free_slots.append(handle.slot)
 
     # ------------------------------------------------------------------ steps
-    def begin_batch(self, handles: Sequence[PagedCacheHandle], query_len: int) -> PagedKVBatch:
-        """Reserve append space and upload one step's page table and lengths."""
+    def begin_batch(self, handles: Sequence[PagedCacheHandle],
+                    query_len: int | Sequence[int]) -> PagedKVBatch:
+        """Reserve append space and upload one step's page table and lengths.
+
+        ``query_len`` is the reference's one chunk length for every request, or a list of
+        one length per request: a packed batch, whose new tokens share one token axis
+        (prefill chunks of any length and one-token decodes in the same forward pass).
+        """
         if not handles:
             raise ValueError("cannot build paged cache metadata for an empty batch")
-        if query_len < 1:
+        packed = not isinstance(query_len, (int, np.integer))
+        if packed:
+            query_lens = [int(n) for n in query_len]
+            if len(query_lens) != len(handles):
+                raise ValueError("a packed batch needs one query length per request")
+        else:
+            query_lens = [int(query_len)] * len(handles)
+        if min(query_lens) < 1:
             raise ValueError("query_len must be positive")
         if any(handle.released for handle in handles):
             raise RuntimeError("cannot use a released cache handle in an attention batch")
@@ -408,7 +475,7 @@ class PagedKVCacheManager:
         if self.page_size < MIN_KV_PAGE_SIZE:
             raise ValueError(f"page_size must be at least {MIN_KV_PAGE_SIZE} tokens")
         lengths = [handle.length for handle in handles]
-        kv_lengths = [length + query_len for length in lengths]
+        kv_lengths = [length + n for length, n in zip(lengths, query_lens)]
         if max(kv_lengths) > self.capacity_tokens:
             raise MemoryError(
                 f"request needs more than the paged cache capacity of {self.capacity_tokens} tokens")
@@ -418,32 +485,63 @@ class PagedKVCacheManager:
             raise MemoryError(
                 f"paged KV cache is full: batch needs {extra} additional pages, "
                 f"but only {len(self._free_pages)} remain")
-        for handle, target in zip(handles, kv_lengths):
+        for handle, target, n in zip(handles, kv_lengths, query_lens):
             self.reserve(handle, target)
-            self._make_writable(handle, handle.length, handle.length + query_len - 1)
+            self._make_writable(handle, handle.length, handle.length + n - 1)
 
         batch = len(handles)
         width = math.ceil(max(kv_lengths) / self.page_size)
         # page-table rows that changed since the last step, then one small upload:
-        # [cache_lens as int64 (2B words) | cache_lens int32 (B) | slots (B)]
+        # [cache_lens as int64 (2B words) | cache_lens int32 (B) | slots (B)], and for a
+        # packed batch [q_start (B) | q_len (B) | decode ids | prefill ids | token rows]
         self._rows.flush()
-        host = np.empty(4 * batch, dtype=np.int32)
+        slots = [handle.slot for handle in handles]
+        if not packed:
+            host = np.empty(4 * batch, dtype=np.int32)
+            host[: 2 * batch].view(np.int64)[:] = lengths
+            host[2 * batch: 3 * batch] = lengths
+            host[3 * batch:] = slots
+            meta = self._uploader.upload(host)
+            table = self._rows.gather(meta[3 * batch:].long(), width)
+            return PagedKVBatch(self, table, meta[: 2 * batch].view(torch.int64),
+                                meta[2 * batch: 3 * batch], query_len, max(kv_lengths), (meta, table))
+        q_len = np.asarray(query_lens, dtype=np.int32)
+        q_start = np.zeros(batch, dtype=np.int32)
+        np.cumsum(q_len[:-1], out=q_start[1:])
+        total = int(q_len.sum())
+        decode_ids = np.nonzero(q_len == 1)[0].astype(np.int32)
+        prefill_ids = np.nonzero(q_len > 1)[0].astype(np.int32)
+        token_request = np.repeat(np.arange(batch, dtype=np.int32), q_len)
+        n_dec = len(decode_ids)
+        host = np.concatenate([np.zeros(2 * batch, dtype=np.int32), np.asarray(lengths, dtype=np.int32),
+                               np.asarray(slots, dtype=np.int32), q_start, q_len, decode_ids,
+                               prefill_ids, token_request])
         host[: 2 * batch].view(np.int64)[:] = lengths
-        host[2 * batch: 3 * batch] = lengths
-        host[3 * batch:] = [handle.slot for handle in handles]
         meta = self._uploader.upload(host)
-        table = self._rows.gather(meta[3 * batch:].long(), width)
-        return PagedKVBatch(self, table, meta[: 2 * batch].view(torch.int64),
-                            meta[2 * batch: 3 * batch], query_len, max(kv_lengths), (meta, table))
+        o = 4 * batch
+        table = self._rows.gather(meta[3 * batch: o].long(), width)
+        layout = PackedLayout(query_lens=query_lens, total_tokens=total,
+                              q_start=meta[o: o + batch], q_len=meta[o + batch: o + 2 * batch],
+                              decode_ids=meta[o + 2 * batch: o + 2 * batch + n_dec],
+                              prefill_ids=meta[o + 2 * batch + n_dec: o + 3 * batch],
+                              token_request=meta[o + 3 * batch:])
+        return PagedKVBatch(self, table, meta[: 2 * batch].view(torch.int64), meta[2 * batch: 3 * batch],
+                            max(query_lens), max(kv_lengths), (meta, table), layout)
 
-    def commit_batch(self, handles: Sequence[PagedCacheHandle], query_len: int) -> None:
+    def commit_batch(self, handles: Sequence[PagedCacheHandle], query_len: int | Sequence[int]) -> None:
         """Advance logical lengths after every layer wrote the step's K/V."""
-        for handle in handles:
+        if isinstance(query_len, (int, np.integer)):
+            query_lens = [int(query_len)] * len(handles)
+        else:
+            query_lens = [int(n) for n in query_len]
+            if len(query_lens) != len(handles):
+                raise ValueError("a packed batch needs one query length per request")
+        for handle, n in zip(handles, query_lens):
             if handle.released:
                 raise RuntimeError("cannot commit a released cache handle")
-            if handle.length + query_len > len(handle.pages) * self.page_size:
+            if handle.length + n > len(handle.pages) * self.page_size:
                 raise RuntimeError("paged cache append space was not reserved")
-            handle.length += query_len
+            handle.length += n
 
     # ------------------------------------------------------------------ helpers
     def workspace_for(self, batch: int, query_len: int, num_q_heads: int, max_kv_len: int):

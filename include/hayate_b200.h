@@ -52,7 +52,8 @@ enum {
   HYT_DEVERR_TABLE_RANGE = 2,  /* kv_len needs more pages than page_table_stride */
   HYT_DEVERR_SPLIT_RANGE = 4,  /* kv_len > max_kv_len given at launch */
   HYT_DEVERR_WAIT_TIMEOUT = 8, /* a bounded pipeline wait gave up */
-  HYT_DEVERR_ISSUE_LANE = 16   /* tensor-core issue ran on other than exactly one lane (work skipped) */
+  HYT_DEVERR_ISSUE_LANE = 16,  /* tensor-core issue ran on other than exactly one lane (work skipped) */
+  HYT_DEVERR_PACKED_RANGE = 32 /* packed batch: q_start/q_len/request id out of range (work skipped) */
 };
 
 /* Message of the last failed call on this thread ("" if none). */
@@ -177,6 +178,62 @@ int hyt_generic_attention(const void* q, const int64_t* q_strides, const void* k
                           int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
                           int32_t page_size, int32_t dtype, float scale,
                           int32_t* error_word, void* stream);
+
+/*
+ * Packed (mixed prefill + decode) batches. No single counterpart in the reference:
+ * its engine runs one forward pass per distinct prefill chunk length plus one for
+ * decoding (hayate/engine/engine.py:226-283, 306-312), each with its own
+ * write_layer/attend_layer calls (paged_cache.py:44-71). Here the new tokens of all
+ * requests share one token axis: request b owns rows q_start[b] .. q_start[b] +
+ * q_len[b] - 1 (total_tokens rows in all), and token_request[i] names the request
+ * of row i. Same slot formula and causal rule as the calls above, per request.
+ */
+
+/* Packed write_layer. new_strides = {k_t, k_h, v_t, v_h} in elements. */
+int hyt_kv_scatter_packed(const void* k_new, const void* v_new, const int64_t* new_strides,
+                          void* k_pool, void* v_pool, int32_t num_layers, int32_t layer,
+                          int64_t capacity_tokens, const int32_t* page_table,
+                          int32_t page_table_stride, const int32_t* cache_lens,
+                          const int32_t* q_start, const int32_t* token_request, int32_t batch,
+                          int32_t total_tokens, int32_t num_kv_heads, int32_t head_dim,
+                          int32_t page_size, int32_t dtype, int32_t* error_word, void* stream);
+
+/* Packed hyt_norm_rope_scatter: qkv_strides = {q_t, q_h, k_t, k_h, v_t, v_h},
+ * q_out_strides = {t, h}; token i is at position cache_lens[b] + i - q_start[b]. */
+int hyt_norm_rope_scatter_packed(const void* q, const void* k, const void* v,
+                                 const int64_t* qkv_strides, const void* q_norm_weight,
+                                 const void* k_norm_weight, float eps, const float* cos,
+                                 const float* sin, int32_t rope_positions, void* q_out,
+                                 const int64_t* q_out_strides, void* k_pool, void* v_pool,
+                                 int32_t num_layers, int32_t layer, int64_t capacity_tokens,
+                                 const int32_t* page_table, int32_t page_table_stride,
+                                 const int32_t* cache_lens, const int32_t* q_start,
+                                 const int32_t* token_request, int32_t batch,
+                                 int32_t total_tokens, int32_t num_q_heads, int32_t num_kv_heads,
+                                 int32_t head_dim, int32_t page_size, int32_t dtype,
+                                 int32_t* error_word, void* stream);
+
+/*
+ * Packed attend_layer in one call: the requests listed in decode_ids (one query
+ * each) go to the split-KV decode kernel, those in prefill_ids (any chunk length up
+ * to max_query_len) to the tcgen05 prefill kernel, both on `stream` (the CUDA-core
+ * kernel serves shapes those two do not take). q_strides/out_strides = {t, h}.
+ * The workspace is the decode kernel's for num_decode requests of one query:
+ * hyt_attention_workspace_bytes(num_decode, 1, ...).
+ */
+int hyt_paged_attention_packed(const void* q, const int64_t* q_strides, const void* k_pool,
+                               const void* v_pool, int32_t num_layers, int32_t layer,
+                               int64_t capacity_tokens, const int32_t* page_table,
+                               int32_t page_table_stride, const int32_t* cache_lens,
+                               const int32_t* q_start, const int32_t* q_len, void* out,
+                               const int64_t* out_strides, int32_t batch, int32_t total_tokens,
+                               int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                               int32_t page_size, int32_t dtype, float scale,
+                               const int32_t* decode_ids, int32_t num_decode,
+                               const int32_t* prefill_ids, int32_t num_prefill,
+                               int32_t max_query_len, int32_t max_kv_len, int32_t split_tokens,
+                               void* workspace, size_t workspace_bytes, int32_t* error_word,
+                               void* stream);
 
 /* Workspace bytes hyt_paged_attention / hyt_decode_attention need for these sizes
  * (0 when the dispatched kernel needs none). split_tokens as in the call. */

@@ -136,3 +136,72 @@ def test_ctypes_types_are_plain():
     for restype, argtypes in _lib.SIGNATURES.values():
         for t in argtypes:
             assert t in (ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t)
+
+
+def _header_types():
+    """ctypes type of every parameter of every declared function, from the header."""
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    out = {}
+    for name in declared_functions():
+        params = re.search(r"\b" + name + r"\s*\((.*?)\);", text, re.S).group(1)
+        types = []
+        for a in (x.strip() for x in params.split(",")):
+            if not a or a == "void":
+                continue
+            if "*" in a:
+                types.append(ctypes.c_void_p)
+            elif a.startswith("int64_t"):
+                types.append(ctypes.c_int64)
+            elif a.startswith("int32_t"):
+                types.append(ctypes.c_int32)
+            elif a.startswith("float"):
+                types.append(ctypes.c_float)
+            elif a.startswith("size_t"):
+                types.append(ctypes.c_size_t)
+            else:
+                raise AssertionError(f"{name}: unexpected parameter {a!r}")
+        out[name] = types
+    return out
+
+
+def test_binding_argument_types_match_the_header():
+    for name, types in _header_types().items():
+        assert list(_lib.SIGNATURES[name][1]) == types, name
+
+
+def _packed_args(**overrides):
+    s = _lib.int64_array([0, 0])
+    args = dict(q=1, qs=s, k_pool=1, v_pool=1, num_layers=1, layer=0, capacity=4096, page_table=1,
+                pts=32, cache_lens=1, q_start=1, q_len=1, out=1, os=s, batch=3, total=10, hq=32,
+                hkv=8, head_dim=128, page_size=128, dtype=0, scale=0.088, dec=1, n_dec=1, pre=1,
+                n_pre=2, max_q=8, max_kv=4096, split=0, ws=None, ws_bytes=0, err=None, stream=None)
+    args.update(overrides)
+    return list(args.values())
+
+
+@pytest.mark.parametrize("bad, message", [
+    (dict(q_start=None), "null pointer"),
+    (dict(n_dec=0, n_pre=0), "at least one request"),
+    (dict(pre=None), "null request list"),
+    (dict(total=0), "total_tokens"),
+    (dict(max_q=11), "max_query_len"),
+    (dict(hq=30), "multiple of num_kv_heads"),
+])
+def test_packed_attention_rejects_bad_arguments(bad, message):
+    lib = _lib.lib()
+    rc = lib.hyt_paged_attention_packed(*_packed_args(**bad))
+    assert rc == -1
+    assert message in lib.hyt_last_error().decode()
+
+
+def test_packed_scatter_rejects_bad_arguments():
+    lib = _lib.lib()
+    s = _lib.int64_array([0, 0, 0, 0])
+    base = [1, 1, s, 1, 1, 1, 0, 1024, 1, 8, 1, 1, 1, 2, 5, 8, 128, 128, 0, None, None]
+    args = list(base)
+    args[12] = None  # token_request
+    assert lib.hyt_kv_scatter_packed(*args) == -1
+    args = list(base)
+    args[14] = 0  # total_tokens
+    assert lib.hyt_kv_scatter_packed(*args) == -1
+    assert "total_tokens" in lib.hyt_last_error().decode()

@@ -216,3 +216,37 @@ def test_persistent_page_table_tracks_every_page_change():
             assert batch.page_table[row].tolist() == expected, (step, row)
         manager.commit_batch(handles, 130)
     assert manager.page_refcount(b.pages[1]) == 1 and b.pages[0] == a.pages[0]
+
+
+def test_packed_batch_layout_and_commit():
+    """One query length per request: a packed batch on one token axis."""
+    manager = make_manager(page_size=128, max_cache_tokens=4096, max_requests=4)
+    a, b, c = manager.allocate(), manager.allocate(), manager.allocate()
+    manager.reserve(a, 300)
+    a.length = 300
+    batch = manager.begin_batch([a, b, c], [1, 130, 5])
+    lay = batch.layout
+    assert lay.query_lens == [1, 130, 5] and lay.total_tokens == 136
+    assert lay.q_start.tolist() == [0, 1, 131] and lay.q_len.tolist() == [1, 130, 5]
+    assert lay.decode_ids.tolist() == [0] and lay.prefill_ids.tolist() == [1, 2]
+    assert lay.token_request.tolist() == [0] + [1] * 130 + [2] * 5
+    assert batch.cache_lens.tolist() == [300, 0, 0] and batch.query_len == 130
+    assert batch.max_kv_len == 301
+    assert [len(h.pages) for h in (a, b, c)] == [3, 2, 1]
+    manager.commit_batch([a, b, c], [1, 130, 5])
+    assert [h.length for h in (a, b, c)] == [301, 130, 5]
+    # a uniform batch after it has no packed layout
+    assert manager.begin_batch([a, b], 2).layout is None
+
+
+def test_packed_batch_argument_errors():
+    manager = make_manager(page_size=128, max_cache_tokens=1024, max_requests=3)
+    a, b = manager.allocate(), manager.allocate()
+    with pytest.raises(ValueError):
+        manager.begin_batch([a, b], [1])
+    with pytest.raises(ValueError):
+        manager.begin_batch([a, b], [1, 0])
+    with pytest.raises(ValueError):
+        manager.commit_batch([a, b], [1, 2, 3])
+    with pytest.raises(MemoryError):
+        manager.begin_batch([a, b], [1, 2000])
