@@ -635,10 +635,13 @@ class _StubTokenizer:
         return ""
 
 
-def run_engine(args, world, rank, impl: str):
+def run_engine(args, world, rank, impl: str, step: str = "reference"):
     """hayate's own Engine and random-init Qwen3-4B (installed from the
     reference into baseline/_ref), with only the paged KV manager swapped: this repo's
-    (impl "ours") or the reference's compiled-FlexAttention one (impl "reference")."""
+    (impl "ours") or the reference's compiled-FlexAttention one (impl "reference").
+    ``step`` "reference" ticks with ``Engine.generate``; "mixed" (ours only) with
+    ``hayate_b200.mixed_step.mixed_generate``: one packed forward pass per group of
+    prompt chunks, decodes included, instead of one per chunk length plus one for decode."""
     import torch
 
     if not os.path.isdir(os.path.join(REF_DIR, "hayate")):
@@ -685,11 +688,17 @@ def run_engine(args, world, rank, impl: str):
             reqs.append(r)
         return reqs
 
+    if step == "mixed":
+        from hayate_b200.mixed_step import mixed_generate
+
+        tick = lambda: mixed_generate(eng)  # noqa: E731
+    else:
+        tick = eng.generate
     with torch.inference_mode():
         # warm-up: library load / FlexAttention compilation on a few shapes
         for _ in range(max(1, args.warmup)):
             submit([700, 33, 1500, 129, 512, 1], 8)
-            while eng.generate():
+            while tick():
                 pass
         lengths = engine_prompt_lengths()
         reqs = submit(lengths, ENGINE_OUTPUT)
@@ -697,7 +706,7 @@ def run_engine(args, world, rank, impl: str):
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0 = time.perf_counter()
         start.record()
-        while eng.generate():
+        while tick():
             pass
         end.record()
         torch.cuda.synchronize()
@@ -714,7 +723,9 @@ def run_engine(args, world, rank, impl: str):
         "config": {"workload": "config 4: hayate Engine, 256 requests, prompts lognormal(median 1024, max 8192), "
                                "256 greedy tokens each, chunk 512, pool 262144 tokens",
                    "max_batch": ENGINE_BATCH, "prompt_tokens": prompt_tokens, "output_tokens": out_tokens,
-                   "kv_manager": "hayate_b200" if impl == "ours" else "reference (torch.compile FlexAttention)"},
+                   "kv_manager": "hayate_b200" if impl == "ours" else "reference (torch.compile FlexAttention)",
+                   "engine_tick": "hayate_b200 mixed_generate (packed prefill + decode passes)"
+                                  if step == "mixed" else "hayate Engine.generate"},
     }
 
 
@@ -778,7 +789,17 @@ def main():
         rank = int(os.environ.get("RANK", "0"))
         if rank == 0:
             try:
-                result = run_engine(args, world, rank, args.impl)
+                if args.impl == "ours":
+                    # the packed tick is this repo's engine step; the reference tick with
+                    # this repo's KV manager is reported beside it
+                    result = run_engine(args, world, rank, "ours", step="mixed")
+                    torch_mod = sys.modules.get("torch")
+                    if torch_mod is not None:
+                        torch_mod.cuda.empty_cache()
+                    ref_tick = run_engine(args, world, rank, "ours", step="reference")
+                    result["reference_tick"] = {k: ref_tick[k] for k in ("value", "total_tok_s", "seconds")}
+                else:
+                    result = run_engine(args, world, rank, args.impl)
             except Exception as exc:  # the reference's torch.compile(flex_attention) path
                 if args.impl != "reference":
                     raise
