@@ -18,8 +18,10 @@
 //     (scale-and-shift and row sums on packed f32x2 pairs, 7 of 8 exponentials on
 //     MUFU and 1 of 8 on the FMA pipe via ex2_poly; masked keys give exact 0 on
 //     both) and writes P as packed bf16/f16 back over its S columns (tcgen05.st).
-//     At the end the pair adds its row sums and each warp normalises and stores
-//     its half of the O rows.
+//     At the end the pair adds its row sums and each warp normalises its half of the
+//     O rows, stages them in shared memory (the idle K/V stages) and stores them with
+//     coalesced 128-byte row segments. Q comes in the same way: one warp load covers
+//     two whole rows.
 //   warp 16 (producer): per 128-key tile looks the page up and TMA-loads K and V
 //     (2 boxes of [128 tokens x 64 dims] each, 128B swizzle) into 2-stage rings,
 //     prefetching the tile kPrefetchTiles ahead into L2.
@@ -67,6 +69,9 @@ constexpr int kVOff = kKOff + 2 * kTileBytes;
 constexpr int kBarOff = kVOff + 2 * kTileBytes;
 constexpr int kRedOff = kBarOff + 256;       // row-max and row-sum exchange, 6 KB
 constexpr int kSmemBytes = kRedOff + 6 * 2 * 128 * 4 + 1024;
+// output staging row (256 B of bf16 plus 16 B so consecutive rows start 4 banks apart)
+constexpr int kStageRowBytes = 272;
+static_assert(2 * kRows * kStageRowBytes <= 4 * kTileBytes, "O staging must fit in the K/V stages");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kOCol = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -347,23 +352,22 @@ __global__ void __maxnreg__(96)
     const int x = warp >> 3, half = (warp >> 2) & 1, quarter = warp & 3;
     const int r = quarter * 32 + lane;  // query row == TMEM lane
     const int t = t0 + r;
-    const bool row_valid = t < query_len;
     const int limit = cache_len + min(t, query_len - 1);  // last visible key
     const uint32_t lane_addr = tmem + (uint32_t(quarter * 32) << 16);
     const int pair_bar = 1 + x * 4 + quarter;  // named barrier of the two warps of this row quarter
     float* red_max = reinterpret_cast<float*>(smem + kRedOff) + x * (2 * 2 * kRows);  // [parity][half][row]
     float* red_sum = reinterpret_cast<float*>(smem + kRedOff) + 2 * (2 * 2 * kRows) + x * (2 * kRows);
 
-    {  // Q rows -> swizzled shared memory: two threads per row, 8 chunks each
-      const int qx = threadIdx.x >> 8, qr = (threadIdx.x >> 1) & 127, qc = (threadIdx.x & 1) * 8;
-      const int qt = t0 + qr;
-      const T* qrow = static_cast<const T*>(p.q) + q_row(qt) + int64_t(h0 + qx) * p.q_sh;
-      uint8_t* qdst = smem + kQOff + qx * kTileBytes;
+    {  // Q rows -> swizzled shared memory; one warp load covers 2 whole rows (512 B)
 #pragma unroll
-      for (int c = qc; c < qc + 8; ++c) {
+      for (int i = 0; i < 8; ++i) {
+        const int idx = i * kSoftmaxThreads + int(threadIdx.x);  // (tile, row, 16-byte chunk)
+        const int c = idx & 15, qr = (idx >> 4) & (kRows - 1), qx = idx >> 11;
+        const int qt = t0 + qr;
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (qt < query_len) v = reinterpret_cast<const uint4*>(qrow)[c];
-        *reinterpret_cast<uint4*>(qdst + sw128_offset(qr, c)) = v;
+        if (qt < query_len)
+          v = reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) + q_row(qt) + int64_t(h0 + qx) * p.q_sh)[c];
+        *reinterpret_cast<uint4*>(smem + kQOff + qx * kTileBytes + sw128_offset(qr, c)) = v;
       }
       fence_proxy_async_smem();
       mbar_arrive(&bars->q_full);
@@ -431,30 +435,38 @@ __global__ void __maxnreg__(96)
       mbar_arrive(&bars->p_full[x]);
     }
 
-    // ---- epilogue: O / l -> out[b, h0 + x, t, half * 64 ..]
+    // ---- epilogue: O / l -> out[b, h0 + x, t, half * 64 ..]. Rows go through shared memory
+    // (the K/V stages are idle once o_done fired) so that each warp store writes four whole
+    // 128-byte row segments instead of 16 bytes of 32 different rows.
     red_sum[half * kRows + r] = l_run;
     mbar_wait(&bars->o_done, 0, err, abort);
     tc_fence_after();
     named_bar_sync(pair_bar, 64);
     const float l = red_sum[r] + red_sum[kRows + r];
     const float inv = l > 0.f ? 1.f / l : 0.f;
-    T* out = static_cast<T*>(p.out) + o_row(t) + int64_t(h0 + x) * p.o_sh + half * 64;
+    uint8_t* stage = smem + kKOff + x * kRows * kStageRowBytes + half * 128;
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       uint32_t o[32];
       tmem_ld32(lane_addr + o_col + c * 32, o);
       tmem_wait_ld();
-      if (row_valid) {
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          uint4 w;
-          w.x = Elem<T>::pack2(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
-          w.y = Elem<T>::pack2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
-          w.z = Elem<T>::pack2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
-          w.w = Elem<T>::pack2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
-          reinterpret_cast<uint4*>(out)[c * 4 + v] = w;
-        }
+      for (int v = 0; v < 4; ++v) {
+        uint4 w;
+        w.x = Elem<T>::pack2(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
+        w.y = Elem<T>::pack2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
+        w.z = Elem<T>::pack2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
+        w.w = Elem<T>::pack2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+        *reinterpret_cast<uint4*>(stage + r * kStageRowBytes + (c * 4 + v) * 16) = w;
       }
+    }
+    __syncwarp();
+    T* out_head = static_cast<T*>(p.out) + int64_t(h0 + x) * p.o_sh + half * 64;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {  // this warp's 32 rows, 4 per store, lane -> 16-byte chunk
+      const int rr = quarter * 32 + i * 4 + (lane >> 3), ch = lane & 7;
+      const uint4 w = *reinterpret_cast<const uint4*>(stage + rr * kStageRowBytes + ch * 16);
+      if (t0 + rr < query_len) reinterpret_cast<uint4*>(out_head + o_row(t0 + rr))[ch] = w;
     }
   }
 
