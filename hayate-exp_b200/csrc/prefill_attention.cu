@@ -358,16 +358,25 @@ __global__ void __maxnreg__(96)
     float* red_max = reinterpret_cast<float*>(smem + kRedOff) + x * (2 * 2 * kRows);  // [parity][half][row]
     float* red_sum = reinterpret_cast<float*>(smem + kRedOff) + 2 * (2 * 2 * kRows) + x * (2 * kRows);
 
-    {  // Q rows -> swizzled shared memory; one warp load covers 2 whole rows (512 B)
+    {  // Q rows -> swizzled shared memory; one warp load covers 2 whole rows (512 B). All
+       // eight loads are issued before the first shared store (one memory round trip, not
+       // eight: the stores would otherwise be ordered behind each load).
+      uint4 v[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int idx = i * kSoftmaxThreads + int(threadIdx.x);  // (tile, row, 16-byte chunk)
         const int c = idx & 15, qr = (idx >> 4) & (kRows - 1), qx = idx >> 11;
         const int qt = t0 + qr;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        v[i] = make_uint4(0u, 0u, 0u, 0u);
         if (qt < query_len)
-          v = reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) + q_row(qt) + int64_t(h0 + qx) * p.q_sh)[c];
-        *reinterpret_cast<uint4*>(smem + kQOff + qx * kTileBytes + sw128_offset(qr, c)) = v;
+          v[i] = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) + q_row(qt) +
+                                                       int64_t(h0 + qx) * p.q_sh) + c);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int idx = i * kSoftmaxThreads + int(threadIdx.x);
+        const int c = idx & 15, qr = (idx >> 4) & (kRows - 1), qx = idx >> 11;
+        *reinterpret_cast<uint4*>(smem + kQOff + qx * kTileBytes + sw128_offset(qr, c)) = v[i];
       }
       fence_proxy_async_smem();
       mbar_arrive(&bars->q_full);
