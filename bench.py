@@ -184,26 +184,25 @@ def barrier(world):
         dist.barrier()
 
 
-def max_over_ranks(value: float, world: int) -> float:
-    if world == 1:
-        return value
+def _reduce(value: float, op_name: str) -> float:
     import torch
     import torch.distributed as dist
 
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    # NCCL reduces device tensors; gloo (the CPU tests of this logic) host tensors
+    device = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=getattr(dist.ReduceOp, op_name))
     return float(t.item())
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    """The slowest rank's time (the job's time): every rank gets the same number."""
+    return value if world == 1 else _reduce(value, "MAX")
 
 
 def sum_over_ranks(value: float, world: int) -> float:
-    if world == 1:
-        return value
-    import torch
-    import torch.distributed as dist
-
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
-    return float(t.item())
+    """Whole-job work (bytes, FLOPs, tokens) from each rank's share."""
+    return value if world == 1 else _reduce(value, "SUM")
 
 
 # ---------------------------------------------------------------------------- decode (cfg 2)
@@ -484,6 +483,12 @@ def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=N
 LONG_GROUPS, LONG_PER_GROUP, LONG_PREFIX, LONG_CONTEXT = 32, 16, 4096, 32768
 
 
+def long_groups(rank: int, world: int) -> list[int]:
+    """Prefix groups of config 5 this rank serves: whole groups, round robin, so every
+    shared prefix stays on one GPU and no data crosses between ranks."""
+    return [g for g in range(LONG_GROUPS) if g % world == rank]
+
+
 def run_longdecode(args, world, rank, local, peaks, peak_kind):
     """512 requests x 32768-token context, groups of 16 alias a 4096-token prefix (shared
     pages); every request decodes one token per step. Groups are split across ranks."""
@@ -493,7 +498,7 @@ def run_longdecode(args, world, rank, local, peaks, peak_kind):
     from hayate_b200 import workloads as W
 
     steps = args.steps
-    groups = [g for g in range(LONG_GROUPS) if g % world == rank]
+    groups = long_groups(rank, world)
     n_req = len(groups) * LONG_PER_GROUP
     own = LONG_CONTEXT - LONG_PREFIX
     unique = len(groups) * (LONG_PREFIX + LONG_PER_GROUP * own)
