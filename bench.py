@@ -89,6 +89,13 @@ DECODE_CFG2_TRAFFIC = 1.217e9
 PREFILL_CFG3_TRAFFIC = 146.12e6
 
 
+def attention_flops(cache_lens, query_len: int, num_q_heads: int, head_dim: int) -> int:
+    """Causal-valid attention FLOPs of a prefill step: 4 * H_q * D per visible (query, key)
+    pair (QK^T and PV, 2 FLOPs per multiply-add), padded tile work not counted."""
+    pairs = sum(int(n) * query_len + query_len * (query_len + 1) // 2 for n in cache_lens)
+    return pairs * 4 * num_q_heads * head_dim
+
+
 def prefill_prefixes(seed: int, batch: int = 8, hi: int = 4096):
     rng = np.random.RandomState(seed)
     return [int(n) for n in rng.randint(0, hi + 1, size=batch)]
@@ -401,7 +408,6 @@ def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=N
     tcgen05 prefill attention."""
     import torch
 
-    import oracle
     from hayate_b200 import PagedKVCacheManager, ops
     from hayate_b200 import workloads as W
 
@@ -420,7 +426,7 @@ def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=N
     q, k, v = W.step_inputs(manager, handles, T, 32, gen)
     batch = manager.begin_batch(handles, T)
     out = torch.empty((len(prefixes), T, 32, 128), dtype=q.dtype, device="cuda").transpose(1, 2)
-    flops = oracle.attention_flops(prefixes, T, 32, 128)
+    flops = attention_flops(prefixes, T, 32, 128)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")  # > 126 MB L2
 
     def step(ev=None):

@@ -61,3 +61,11 @@ def test_flops_and_bytes_formulas():
     assert oracle.attention_flops([0], 1, 32, 128) == 4 * 32 * 128
     assert oracle.attention_flops([10], 4, 1, 1) == 4 * (40 + 10)
     assert oracle.decode_bytes([512, 512], 8, 128) == 1024 * 8 * 128 * 2 * 2
+
+
+def test_bench_flop_count_matches_the_oracle():
+    """bench.py counts prefill FLOPs itself (its GPU legs do not touch oracle/)."""
+    import bench
+
+    for lens, t in (([2998, 4045, 1590, 2020, 1436, 3762, 183, 2532], 512), ([0], 1), ([5, 0, 77], 130)):
+        assert bench.attention_flops(lens, t, 32, 128) == oracle.attention_flops(lens, t, 32, 128)
