@@ -86,7 +86,7 @@ def decode_lengths(seed: int, batch: int = 64, lo: int = 1024, hi: int = 8192):
 # from one ncu capture each: config 2 decode scaled from a 16-request capture by kv tokens
 # (1.028 x the algorithmic bytes), config 3 prefill captured at full size.
 DECODE_CFG2_TRAFFIC = 1.217e9
-PREFILL_CFG3_TRAFFIC = 146.12e6
+PREFILL_CFG3_TRAFFIC = 144.89e6
 
 
 def attention_flops(cache_lens, query_len: int, num_q_heads: int, head_dim: int) -> int:
@@ -331,45 +331,93 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
 
 
 def decode_e2e(args, world, manager, handles, ctx, q, k, v, step_bytes):
-    """Same step through the public API with host buffers: H2D inputs, D2H output."""
+    """Same step through the public API with host buffers: each step copies its inputs
+    host -> device and its output device -> host (pinned memory), inside the timed region.
+
+    Measured twice: serial (copy in, compute, copy out, one stream) and pipelined the way a
+    serving loop feeds the engine (a copy stream brings step i+1's inputs in and takes step
+    i's output out while step i+1 / i computes; double-buffered device inputs). ``value`` is
+    the pipelined figure; both are reported."""
     import torch
 
+    B = len(ctx)
     q_h = q.detach().cpu().pin_memory()
     k_h = k.detach().cpu().pin_memory()
     v_h = v.detach().cpu().pin_memory()
-    out_h = torch.empty((len(ctx), 32, 1, 128), dtype=q.dtype).pin_memory()
+    out_h = [torch.empty((B, 32, 1, 128), dtype=q.dtype).pin_memory() for _ in range(2)]
+    dev = [tuple(torch.empty_like(t, device="cuda") for t in (q, k, v)) for _ in range(2)]
+    meta_bytes = (3 * B + B * max(len(h.pages) for h in handles)) * 4
+    total = sum_over_ranks(float(step_bytes), world)
 
-    def step():
+    def serial_step():
         batch = manager.begin_batch(handles, 1)               # H2D: page table + lengths
         qd = q_h.to("cuda", non_blocking=True)
         kd = k_h.to("cuda", non_blocking=True)
         vd = v_h.to("cuda", non_blocking=True)
         batch.write_layer(0, kd, vd)
         o = batch.attend_layer(qd, 0)
-        out_h.copy_(o, non_blocking=True)                     # D2H of the step's result
-        return batch
+        out_h[0].copy_(o, non_blocking=True)                  # D2H of the step's result
+
+    compute = torch.cuda.current_stream()
+    copier = torch.cuda.Stream()
+    inputs_ready = [torch.cuda.Event() for _ in range(2)]
+    inputs_free = [torch.cuda.Event() for _ in range(2)]
+    output_ready = [torch.cuda.Event() for _ in range(2)]
+
+    def copy_in(i):
+        s = i & 1
+        with torch.cuda.stream(copier):
+            copier.wait_event(inputs_free[s])
+            for dst, src in zip(dev[s], (q_h, k_h, v_h)):
+                dst.copy_(src, non_blocking=True)
+            inputs_ready[s].record(copier)
+
+    def pipelined(steps):
+        for s in range(2):
+            inputs_free[s].record(compute)
+        copy_in(0)
+        for i in range(steps):
+            s = i & 1
+            if i + 1 < steps:
+                copy_in(i + 1)
+            compute.wait_event(inputs_ready[s])
+            batch = manager.begin_batch(handles, 1)
+            qd, kd, vd = dev[s]
+            batch.write_layer(0, kd, vd)
+            o = batch.attend_layer(qd, 0)
+            inputs_free[s].record(compute)
+            output_ready[s].record(compute)
+            with torch.cuda.stream(copier):
+                copier.wait_stream(compute)
+                out_h[s].copy_(o, non_blocking=True)
+        compute.wait_stream(copier)
+
+    def timed(fn):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record()
+        fn()
+        end.record()
+        torch.cuda.synchronize()
+        barrier(world)
+        return max_over_ranks(start.elapsed_time(end), world)
 
     for _ in range(max(3, args.warmup)):
-        step()
+        serial_step()
+    pipelined(max(3, args.warmup))
     torch.cuda.synchronize()
-    meta_bytes = (3 * len(ctx) + len(ctx) * max(len(h.pages) for h in handles)) * 4
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize()
-    start.record()
-    for _ in range(args.steps):
-        step()
-    end.record()
-    torch.cuda.synchronize()
-    barrier(world)
-    ms = max_over_ranks(start.elapsed_time(end), world)
-    total = sum_over_ranks(float(step_bytes), world)
+    ms_serial = timed(lambda: [serial_step() for _ in range(args.steps)])
+    ms_pipe = timed(lambda: pipelined(args.steps))
     manager.check_device_errors()
-    return {"value": round(total * args.steps / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
-            "ms_per_step": round(ms / args.steps, 4),
+    return {"value": round(total * args.steps / (ms_pipe / 1e3) / 1e9, 1), "unit": "GB/s",
+            "ms_per_step": round(ms_pipe / args.steps, 4),
+            "serial": {"value": round(total * args.steps / (ms_serial / 1e3) / 1e9, 1),
+                       "ms_per_step": round(ms_serial / args.steps, 4)},
             "h2d_bytes_per_step": int(q_h.numel() * 2 + k_h.numel() * 2 + v_h.numel() * 2 + meta_bytes),
-            "d2h_bytes_per_step": int(out_h.numel() * 2),
-            "path": "PagedKVCacheManager.begin_batch -> write_layer -> attend_layer, pinned host buffers"}
+            "d2h_bytes_per_step": int(out_h[0].numel() * 2),
+            "path": "PagedKVCacheManager.begin_batch -> write_layer -> attend_layer, pinned host "
+                    "buffers; copies on a second stream overlap the neighbouring steps"}
 
 
 def cpu_threads() -> int:
