@@ -59,6 +59,7 @@ class PagedCacheHandle:
     pages: list[int] = field(default_factory=list)
     length: int = 0
     released: bool = False
+    aliased: bool = False  # some page may be shared with another request (set by share)
 
 
 class _MetaUploader:
@@ -365,6 +366,8 @@ class PagedKVCacheManager:
             self._page_refs[page] += 1
         handle.pages = list(pages)
         handle.length = num_tokens
+        if pages:
+            handle.aliased = source.aliased = True
         self._rows.set_row(handle.slot, handle.pages)
         return handle
 
@@ -446,6 +449,7 @@ class PagedKVCacheManager:
         self._rows.set_row(handle.slot, ())
         handle.length = 0
         handle.released = True
+        handle.aliased = False
         self._free_slots.append(handle.slot)
 
     # ------------------------------------------------------------------ steps
@@ -474,20 +478,27 @@ class PagedKVCacheManager:
             raise ValueError("an attention batch cannot contain the same cache handle twice")
         if self.page_size < MIN_KV_PAGE_SIZE:
             raise ValueError(f"page_size must be at least {MIN_KV_PAGE_SIZE} tokens")
+        size = self.page_size
         lengths = [handle.length for handle in handles]
         kv_lengths = [length + n for length, n in zip(lengths, query_lens)]
         if max(kv_lengths) > self.capacity_tokens:
             raise MemoryError(
                 f"request needs more than the paged cache capacity of {self.capacity_tokens} tokens")
-        extra = sum(max(0, math.ceil(n / self.page_size) - len(h.pages))
-                    for h, n in zip(handles, kv_lengths))
+        # only requests whose appends cross into a page they do not hold yet need pages
+        # (a decode step inside its last page needs none: the common case stays cheap)
+        growing = [(h, n) for h, n in zip(handles, kv_lengths) if n > len(h.pages) * size]
+        extra = sum(-(-n // size) - len(h.pages) for h, n in growing)
         if extra > len(self._free_pages):
             raise MemoryError(
                 f"paged KV cache is full: batch needs {extra} additional pages, "
                 f"but only {len(self._free_pages)} remain")
-        for handle, target, n in zip(handles, kv_lengths, query_lens):
+        for handle, target in growing:
             self.reserve(handle, target)
-            self._make_writable(handle, handle.length, handle.length + n - 1)
+        # copy-on-write where an append lands in a page another request still holds (only
+        # requests that took part in share() can hold such pages)
+        for handle, length, n in zip(handles, lengths, query_lens):
+            if handle.aliased:
+                self._make_writable(handle, length, length + n - 1)
 
         batch = len(handles)
         width = math.ceil(max(kv_lengths) / self.page_size)

@@ -250,3 +250,21 @@ def test_packed_batch_argument_errors():
         manager.commit_batch([a, b], [1, 2, 3])
     with pytest.raises(MemoryError):
         manager.begin_batch([a, b], [1, 2000])
+
+
+def test_copy_on_write_follows_sharing_only():
+    """Requests that never shared pages skip the copy-on-write check; shared ones get it."""
+    manager = PagedKVCacheManager(1, 1, 4, 2048, 128, 6, torch.float32, "cpu")
+    values = torch.randn(1, 1, 200, 4)
+    a = manager.allocate_for_request(Cache.from_tensors(values, values))
+    plain = manager.allocate_for_request(Cache.from_tensors(values, values))
+    assert not a.aliased and not plain.aliased
+    twin = manager.share(a, 150)
+    assert a.aliased and twin.aliased and not plain.aliased
+    empty = manager.share(plain, 0)           # nothing aliased: flags unchanged
+    assert not plain.aliased and not empty.aliased
+    shared_page = twin.pages[1]
+    manager.begin_batch([a, twin, plain], [1, 1, 1])
+    assert twin.pages[1] != shared_page and a.pages[1] == shared_page
+    manager.release(twin)
+    assert not twin.aliased
