@@ -265,6 +265,9 @@ def test_copy_on_write_follows_sharing_only():
     assert not plain.aliased and not empty.aliased
     shared_page = twin.pages[1]
     manager.begin_batch([a, twin, plain], [1, 1, 1])
-    assert twin.pages[1] != shared_page and a.pages[1] == shared_page
+    # both append into the shared second page: the first to write (a) gets a copy
+    assert a.pages[1] != shared_page and twin.pages[1] == shared_page
+    assert manager.page_refcount(a.pages[1]) == 1 and manager.page_refcount(shared_page) == 1
+    assert a.pages[0] == twin.pages[0] and manager.page_refcount(a.pages[0]) == 2
     manager.release(twin)
     assert not twin.aliased
