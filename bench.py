@@ -747,10 +747,11 @@ def run_engine(args, world, rank, impl: str, step: str = "reference"):
             reqs.append(r)
         return reqs
 
-    if step == "mixed":
-        from hayate_b200.mixed_step import mixed_generate
+    if step in ("mixed", "graphs"):
+        from hayate_b200.mixed_step import DecodeGraphs, mixed_generate
 
-        tick = lambda: mixed_generate(eng)  # noqa: E731
+        graphs = DecodeGraphs(eng) if step == "graphs" else None
+        tick = lambda: mixed_generate(eng, graphs)  # noqa: E731
     else:
         tick = eng.generate
     with torch.inference_mode():
@@ -783,8 +784,9 @@ def run_engine(args, world, rank, impl: str, step: str = "reference"):
                                "256 greedy tokens each, chunk 512, pool 262144 tokens",
                    "max_batch": ENGINE_BATCH, "prompt_tokens": prompt_tokens, "output_tokens": out_tokens,
                    "kv_manager": "hayate_b200" if impl == "ours" else "reference (torch.compile FlexAttention)",
-                   "engine_tick": "hayate_b200 mixed_generate (packed prefill + decode passes)"
-                                  if step == "mixed" else "hayate Engine.generate"},
+                   "engine_tick": {"mixed": "hayate_b200 mixed_generate (packed prefill + decode passes)",
+                                   "graphs": "hayate_b200 mixed_generate, decode-only ticks replayed from "
+                                             "CUDA graphs (DecodeGraphs)"}.get(step, "hayate Engine.generate")},
     }
 
 
@@ -849,14 +851,16 @@ def main():
         if rank == 0:
             try:
                 if args.impl == "ours":
-                    # the packed tick is this repo's engine step; the reference tick with
-                    # this repo's KV manager is reported beside it
-                    result = run_engine(args, world, rank, "ours", step="mixed")
-                    torch_mod = sys.modules.get("torch")
-                    if torch_mod is not None:
-                        torch_mod.cuda.empty_cache()
-                    ref_tick = run_engine(args, world, rank, "ours", step="reference")
-                    result["reference_tick"] = {k: ref_tick[k] for k in ("value", "total_tok_s", "seconds")}
+                    # this repo's engine step (packed passes, graph-replayed decode ticks);
+                    # beside it the packed step without graphs and hayate's own tick, both
+                    # on this repo's KV manager
+                    result = run_engine(args, world, rank, "ours", step="graphs")
+                    for name, step in (("packed_tick", "mixed"), ("reference_tick", "reference")):
+                        torch_mod = sys.modules.get("torch")
+                        if torch_mod is not None:
+                            torch_mod.cuda.empty_cache()
+                        other = run_engine(args, world, rank, "ours", step=step)
+                        result[name] = {k: other[k] for k in ("value", "total_tok_s", "seconds")}
                 else:
                     result = run_engine(args, world, rank, args.impl)
             except Exception as exc:  # the reference's torch.compile(flex_attention) path

@@ -96,6 +96,16 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
 }
 
 // ---------------------------------------------------------------- TMA
+// Raise a kernel's dynamic shared-memory limit, except while `stream` is being captured
+// into a CUDA graph (the same launch ran uncaptured first, which set it on this device).
+template <typename Kernel>
+inline cudaError_t allow_smem(Kernel kernel, int bytes, cudaStream_t stream) {
+  cudaStreamCaptureStatus status = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &status) == cudaSuccess && status != cudaStreamCaptureStatusNone)
+    return cudaSuccess;
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
 // 3-D tiled load into this CTA's shared memory, completing on an mbarrier.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int c0, int c1, int c2) {

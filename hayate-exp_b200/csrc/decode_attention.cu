@@ -380,12 +380,12 @@ cudaError_t run_decode_attention(const AttentionParams& p, const DecodeLaunch& d
   const dim3 grid(unsigned(d.max_splits), unsigned(p.num_kv_heads), unsigned(att_launch_count(p)));
   if (dtype == HYT_DTYPE_F16) {
     auto kernel = decode_attention_kernel<__half>;
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    cudaError_t err = allow_smem(kernel, kSmemBytes, stream);
     if (err != cudaSuccess) return err;
     kernel<<<grid, kThreads, kSmemBytes, stream>>>(k_map, v_map, P);
   } else {
     auto kernel = decode_attention_kernel<__nv_bfloat16>;
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    cudaError_t err = allow_smem(kernel, kSmemBytes, stream);
     if (err != cudaSuccess) return err;
     kernel<<<grid, kThreads, kSmemBytes, stream>>>(k_map, v_map, P);
   }

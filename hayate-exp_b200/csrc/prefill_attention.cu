@@ -498,7 +498,7 @@ cudaError_t run_prefill_attention(const AttentionParams& p, const CUtensorMap& k
   const dim3 grid(unsigned((p.query_len + kRows - 1) / kRows), unsigned(p.num_q_heads / 2),
                   unsigned(att_launch_count(p)));
   auto launch = [&](auto kernel) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    cudaError_t e = allow_smem(kernel, kSmemBytes, stream);
     if (e != cudaSuccess) return e;
     kernel<<<grid, kThreads, kSmemBytes, stream>>>(k_map, v_map, P);
     return cudaSuccess;

@@ -111,10 +111,86 @@ def _run_group(engine, prefill, decode, device):
             engine._store_prompt_prefix(request)
 
 
-def mixed_generate(engine) -> bool:
+class DecodeGraphs:
+    """Decode-only ticks replayed from CUDA graphs.
+
+    Once every active request is decoding, a tick is the same short forward pass over a
+    few dozen tokens; run eagerly, its ~20 launches per layer cost more host time than the
+    GPU needs. Here each (batch size bucket, longest-context bucket) gets one graph of
+    ``packed_forward`` over a ``StaticDecodeBatch`` (captured on first use); a tick copies
+    the tokens and the page metadata into the graph's buffers and replays it. Requests
+    beyond the real batch are padding rows on the manager's scratch page, their scores
+    discarded. Sampling, ``finalize`` and the page bookkeeping are ``decode_batch``'s
+    (``engine.py:285-296``).
+    """
+
+    def __init__(self, engine, sizes=(8, 16, 32, 48, 64, 96, 128),
+                 kv_buckets=(2048, 4096, 8192, 16384, 32768)):
+        self.engine = engine
+        manager = engine.paged_cache
+        limit = min(manager.capacity_tokens, engine.max_position_embeddings)
+        self.sizes = sorted({n for n in sizes if n < manager.max_requests} | {manager.max_requests})
+        self.kv_buckets = sorted({min(k, limit) for k in kv_buckets} | {limit})
+        self.graphs: dict = {}
+        self.device = manager.device
+
+    def _graph(self, n: int, max_kv: int):
+        size = next((s for s in self.sizes if s >= n), None)
+        kv = next((k for k in self.kv_buckets if k >= max_kv), None)
+        if size is None or kv is None:
+            return None
+        key = (size, kv)
+        if key not in self.graphs:
+            self.graphs[key] = self._capture(size, kv)
+        return self.graphs[key]
+
+    def _capture(self, size: int, kv: int):
+        model = self.engine.model
+        static = self.engine.paged_cache.static_decode_batch(size, kv, model.layers[0].self_attn.num_heads)
+        tokens = torch.zeros(size, dtype=torch.long, device=self.device)
+        rows = torch.arange(size, device=self.device)
+        host_tokens = torch.zeros(size, dtype=torch.long, pin_memory=True)
+        static.update([])  # all padding while capturing
+        with torch.inference_mode():
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):  # warm-up outside the capture (library set-up)
+                for _ in range(2):
+                    packed_forward(model, tokens, static.batch, rows)
+            torch.cuda.current_stream().wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                logits = packed_forward(model, tokens, static.batch, rows)
+        return graph, static, tokens, host_tokens, logits
+
+    def step(self, decode) -> bool:
+        """Run one decode tick for ``decode`` from a graph; False if no bucket fits."""
+        handles = [request.paged_cache for request in decode]
+        if any(h is None for h in handles):
+            raise RuntimeError("every request must own paged KV storage before inference")
+        n = len(decode)
+        found = self._graph(n, max(h.length for h in handles) + 1)
+        if found is None:
+            return False
+        graph, static, tokens, host_tokens, logits = found
+        torch.cuda.current_stream().synchronize()  # the pinned token buffer is reused
+        host_tokens.zero_()
+        host_tokens[:n] = torch.tensor([request.tokens[-1] for request in decode])
+        static.update(handles)
+        tokens.copy_(host_tokens, non_blocking=True)
+        graph.replay()
+        self.engine.paged_cache.commit_batch(handles, 1)
+        next_tokens = self.engine.sampler.sample(logits[:n], decode).flatten().tolist()
+        for request, token in zip(decode, next_tokens):
+            self.engine.sampler.finalize(request, token)
+        return True
+
+
+def mixed_generate(engine, graphs: DecodeGraphs | None = None) -> bool:
     """Run one scheduler tick of ``engine`` (a hayate ``Engine`` whose ``paged_cache`` is a
     ``hayate_b200.PagedKVCacheManager``) with packed forward passes; return whether any
-    request remains active (``Engine.generate``'s contract)."""
+    request remains active (``Engine.generate``'s contract). With ``graphs``, ticks in which
+    every request decodes replay a CUDA graph."""
     previous = list(engine.scheduler.current_batch)
     batch = engine.scheduler.tick()
     active = {id(request) for request in batch}
@@ -125,6 +201,8 @@ def mixed_generate(engine) -> bool:
         return False
     prefill = [r for r in batch if r.is_prefill]
     decode = [r for r in batch if not r.is_prefill]
+    if graphs is not None and not prefill and graphs.step(decode):
+        return True
     device = engine.paged_cache.device
     groups = [prefill[i:i + MAX_PREFILL_BATCH] for i in range(0, len(prefill), MAX_PREFILL_BATCH)] or [[]]
     for index, group in enumerate(groups):

@@ -185,7 +185,7 @@ class PagedKVBatch:
     """
 
     __slots__ = ("k_cache", "v_cache", "page_table", "cache_lens", "page_size", "query_len",
-                 "max_kv_len", "cache_lens_i32", "layout", "_manager", "_meta")
+                 "max_kv_len", "cache_lens_i32", "layout", "workspace", "_manager", "_meta")
 
     def __init__(self, manager, page_table, cache_lens, cache_lens_i32, query_len, max_kv_len, meta,
                  layout: PackedLayout | None = None):
@@ -198,6 +198,7 @@ class PagedKVBatch:
         self.query_len = query_len
         self.max_kv_len = max_kv_len
         self.layout = layout
+        self.workspace = None  # a batch with a fixed workspace (graph replays) sets its own
         self._manager = manager
         self._meta = meta  # keeps the uploaded buffer alive while kernels read it
 
@@ -249,7 +250,9 @@ class PagedKVBatch:
             if q.shape[0] != 1 or q.shape[2] != lay.total_tokens:
                 raise ValueError("a packed batch's q is [1, H_q, total_tokens, head_dim]")
             n_dec = lay.decode_ids.numel()
-            workspace = manager.workspace_for(n_dec, 1, q.shape[1], self.max_kv_len) if n_dec else None
+            workspace = self.workspace
+            if workspace is None and n_dec:
+                workspace = manager.workspace_for(n_dec, 1, q.shape[1], self.max_kv_len)
             return ops.paged_attention_packed(
                 q, self.k_cache, self.v_cache, layer_idx, self.page_table, self.cache_lens_i32,
                 lay.q_start, lay.q_len, lay.decode_ids, lay.prefill_ids, self.page_size,
@@ -272,6 +275,73 @@ class PagedKVBatch:
         ops.kv_scatter_packed(k, v, self.k_cache, self.v_cache, layer_idx, self.page_table,
                               self.cache_lens_i32, lay.q_start, lay.token_request, self.page_size,
                               error_word=self._manager.error_word)
+
+
+class StaticDecodeBatch:
+    """A packed one-token-per-request batch of fixed size whose device buffers never move,
+    for capturing a decode step in a CUDA graph and replaying it every tick.
+
+    ``update(handles)`` (at most ``size`` requests, each with cache length + 1 <=
+    ``max_kv_len``) does the step's page bookkeeping (``begin_batch``'s) and copies the
+    lengths, slots and page rows into the buffers on the current stream. Rows past the real
+    requests are padding: length 0 on the manager's scratch page, which nothing else uses,
+    so their (discarded) writes and reads stay inside the pool.
+    """
+
+    def __init__(self, manager: "PagedKVCacheManager", size: int, max_kv_len: int, num_q_heads: int):
+        if size < 1 or max_kv_len < 1 or max_kv_len > manager.capacity_tokens:
+            raise ValueError("static batch size and max_kv_len must be positive and within the pool")
+        device = manager.device
+        self.size, self.max_kv_len = size, max_kv_len
+        self.width = -(-max_kv_len // manager.page_size)
+        manager._ensure_scratch_page()
+        manager._rows._ensure_width(self.width)
+        self.meta = torch.zeros(4 * size, dtype=torch.int32, device=device)  # [lens64 | lens32 | slots]
+        self.table = torch.full((size, self.width), -1, dtype=torch.int32, device=device)
+        rows = torch.arange(size, dtype=torch.int32, device=device)
+        layout = PackedLayout(query_lens=[1] * size, total_tokens=size, q_start=rows,
+                              q_len=torch.ones(size, dtype=torch.int32, device=device),
+                              token_request=rows, decode_ids=rows, prefill_ids=rows[:0])
+        self.batch = PagedKVBatch(manager, self.table, self.meta[: 2 * size].view(torch.int64),
+                                  self.meta[2 * size: 3 * size], 1, max_kv_len, (self.meta, self.table),
+                                  layout)
+        need = ops.attention_workspace_bytes(size, 1, num_q_heads, manager.num_kv_heads,
+                                             manager.head_dim, max_kv_len, manager.k_cache.dtype,
+                                             manager.split_tokens)
+        self.batch.workspace = ops.new_workspace(need, device) if need else None
+        pin = device.type == "cuda"
+        self._staging = [torch.empty(4 * size, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
+        self._events: list = [None, None]
+        self._flip = 0
+        self._manager = manager
+
+    def update(self, handles: Sequence[PagedCacheHandle]) -> None:
+        m = self._manager
+        n = len(handles)
+        if n > self.size:
+            raise ValueError(f"static batch holds {self.size} requests, got {n}")
+        if n:
+            m._prepare_step(handles, 1, False)
+        lengths = [h.length for h in handles]
+        if n and max(lengths) + 1 > self.max_kv_len:
+            raise ValueError("a request outgrew the static batch's max_kv_len")
+        m._rows.flush()
+        i = self._flip
+        self._flip ^= 1
+        if self._events[i] is not None:
+            self._events[i].synchronize()
+        host = self._staging[i]
+        pad = self.size - n
+        lens = np.asarray(lengths + [0] * pad, dtype=np.int64)
+        h = host.numpy()
+        h[: 2 * self.size].view(np.int64)[:] = lens
+        h[2 * self.size: 3 * self.size] = lens
+        h[3 * self.size:] = [handle.slot for handle in handles] + [m.max_requests] * pad
+        self.meta.copy_(host, non_blocking=True)
+        if m.device.type == "cuda":
+            self._events[i] = torch.cuda.Event()
+            self._events[i].record()
+        torch.index_select(m._rows.dev[:, : self.width], 0, self.meta[3 * self.size:].long(), out=self.table)
 
 
 class PagedKVCacheManager:
@@ -304,7 +374,9 @@ class PagedKVCacheManager:
         self.error_word = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._workspace: torch.Tensor | None = None
         self._uploader = _MetaUploader(self.device)
-        self._rows = _SlotPageTable(max_requests, self.device)
+        # one row past the request slots: the padding row of fixed-size (graph) batches
+        self._rows = _SlotPageTable(max_requests + 1, self.device)
+        self._scratch_page: int | None = None
         self.kernel = "auto"     # pin a kernel ("decode", "prefill", "generic") for testing
         self.split_tokens = 0    # 0 lets the library pick the decode split size
 
@@ -453,17 +525,9 @@ class PagedKVCacheManager:
         self._free_slots.append(handle.slot)
 
     # ------------------------------------------------------------------ steps
-    def begin_batch(self, handles: Sequence[PagedCacheHandle],
-                    query_len: int | Sequence[int]) -> PagedKVBatch:
-        """Reserve append space and upload one step's page table and lengths.
-
-        ``query_len`` is the reference's one chunk length for every request, or a list of
-        one length per request: a packed batch, whose new tokens share one token axis
-        (prefill chunks of any length and one-token decodes in the same forward pass).
-        """
-        if not handles:
-            raise ValueError("cannot build paged cache metadata for an empty batch")
-        packed = not isinstance(query_len, (int, np.integer))
+    def _prepare_step(self, handles, query_len, packed: bool):
+        """Validate a step, reserve its append space and copy shared pages it writes into;
+        returns (cache lengths, query lengths, kv lengths) per request."""
         if packed:
             query_lens = [int(n) for n in query_len]
             if len(query_lens) != len(handles):
@@ -499,6 +563,21 @@ class PagedKVCacheManager:
         for handle, length, n in zip(handles, lengths, query_lens):
             if handle.aliased:
                 self._make_writable(handle, length, length + n - 1)
+
+        return lengths, query_lens, kv_lengths
+
+    def begin_batch(self, handles: Sequence[PagedCacheHandle],
+                    query_len: int | Sequence[int]) -> PagedKVBatch:
+        """Reserve append space and upload one step's page table and lengths.
+
+        ``query_len`` is the reference's one chunk length for every request, or a list of
+        one length per request: a packed batch, whose new tokens share one token axis
+        (prefill chunks of any length and one-token decodes in the same forward pass).
+        """
+        if not handles:
+            raise ValueError("cannot build paged cache metadata for an empty batch")
+        packed = not isinstance(query_len, (int, np.integer))
+        lengths, query_lens, kv_lengths = self._prepare_step(handles, query_len, packed)
 
         batch = len(handles)
         width = math.ceil(max(kv_lengths) / self.page_size)
@@ -553,6 +632,20 @@ class PagedKVCacheManager:
             if handle.length + n > len(handle.pages) * self.page_size:
                 raise RuntimeError("paged cache append space was not reserved")
             handle.length += n
+
+    # ------------------------------------------------------------------ fixed-size batches
+    def _ensure_scratch_page(self) -> None:
+        """One page held for good, read and written only by padding rows of fixed-size
+        batches (the spare slot row past the request slots points at it)."""
+        if self._scratch_page is None:
+            if not self._free_pages:
+                raise MemoryError("paged KV cache is full: no page left for the padding row")
+            self._scratch_page = self._take_pages(1)[0]
+            self._rows.set_row(self.max_requests, [self._scratch_page])
+
+    def static_decode_batch(self, size: int, max_kv_len: int, num_q_heads: int) -> StaticDecodeBatch:
+        """A fixed-size decode batch for CUDA-graph capture (see ``StaticDecodeBatch``)."""
+        return StaticDecodeBatch(self, size, max_kv_len, num_q_heads)
 
     # ------------------------------------------------------------------ helpers
     def workspace_for(self, batch: int, query_len: int, num_q_heads: int, max_kv_len: int):

@@ -11,7 +11,7 @@ import pytest
 import torch
 
 from hayate_b200 import PagedKVCacheManager
-from hayate_b200.mixed_step import mixed_generate, packed_forward
+from hayate_b200.mixed_step import DecodeGraphs, mixed_generate, packed_forward
 
 pytestmark = pytest.mark.gpu
 
@@ -75,9 +75,8 @@ def test_packed_forward_matches_model_forward(model):
     assert (a.argmax(-1) == b.argmax(-1)).float().mean().item() >= 0.75
 
 
-def test_mixed_generate_runs_requests_to_completion(model):
+def make_engine(model, max_batch=6):
     from hayate.engine import engine as ref_engine
-    from hayate.engine.request import Request
     from hayate.engine.sampler import Sampler
     from hayate.engine.scheduler import Scheduler
 
@@ -97,23 +96,68 @@ def test_mixed_generate_runs_requests_to_completion(model):
     eng.max_position_embeddings = model.max_position_embeddings
     eng.tokenizer = _Tok()
     eng.stop_token_ids = set()
-    eng.scheduler = Scheduler(max_batch_size=6)
+    eng.scheduler = Scheduler(max_batch_size=max_batch)
     eng.prefix_cache = None
     eng.sampler = Sampler(eng.tokenizer, set())
-    eng.paged_cache = manager_for(model, requests=6)
-    gen = torch.Generator().manual_seed(2)
+    eng.paged_cache = manager_for(model, requests=max_batch)
+    return eng
+
+
+def submit(eng, lengths, max_tokens, seed=2):
+    from hayate.engine.request import Request
+
+    gen = torch.Generator().manual_seed(seed)
     reqs = []
-    for i, n in enumerate((5, 300, 129, 1, 700, 64, 33, 250)):
-        r = Request(id=i, prompt_tokens=torch.randint(0, 151936, (n,), generator=gen).tolist(), max_tokens=6)
+    for i, n in enumerate(lengths):
+        r = Request(id=i, prompt_tokens=torch.randint(0, 151936, (n,), generator=gen).tolist(), max_tokens=max_tokens)
         eng._prepare_request(r)
         eng.scheduler.add(r)
         reqs.append(r)
+    return reqs
+
+
+@pytest.mark.parametrize("use_graphs", [False, True], ids=["eager", "graphs"])
+def test_mixed_generate_runs_requests_to_completion(model, use_graphs):
+    eng = make_engine(model)
+    graphs = DecodeGraphs(eng, sizes=(4, 8), kv_buckets=(1024,)) if use_graphs else None
+    reqs = submit(eng, (5, 300, 129, 1, 700, 64, 33, 250), 6)
     ticks = 0
     with torch.inference_mode():
-        while mixed_generate(eng):
+        while mixed_generate(eng, graphs):
             ticks += 1
             assert ticks < 200
     torch.cuda.synchronize()
     eng.paged_cache.check_device_errors()
     assert all(r.is_completed and len(r.tokens) == 6 for r in reqs)
-    assert len(eng.paged_cache._free_pages) == eng.paged_cache.num_pages  # every page returned
+    held = 1 if use_graphs else 0  # the padding rows' scratch page stays with the manager
+    assert len(eng.paged_cache._free_pages) == eng.paged_cache.num_pages - held
+    if use_graphs:
+        assert graphs.graphs, "no decode tick was replayed from a graph"
+
+
+def test_decode_graph_matches_eager_forward(model):
+    """A graph-replayed decode step (padded to its bucket) scores like the eager packed pass."""
+    eng = make_engine(model, max_batch=6)
+    reqs = submit(eng, (40, 300, 129, 7, 500), 50, seed=5)
+    with torch.inference_mode():
+        while any(r.is_prefill for r in reqs):
+            mixed_generate(eng)
+        decode = [r for r in reqs if not r.is_completed]
+        handles = [r.paged_cache for r in decode]
+        n = len(decode)
+        tokens = torch.tensor([r.tokens[-1] for r in decode], device="cuda")
+        batch = eng.paged_cache.begin_batch(handles, [1] * n)
+        eager = packed_forward(model, tokens, batch, torch.arange(n, device="cuda")).float()
+        graphs = DecodeGraphs(eng, sizes=(8,), kv_buckets=(2048,))
+        graph, static, tok_buf, host_tokens, logits = graphs._graph(n, max(h.length for h in handles) + 1)
+        host_tokens.zero_()
+        host_tokens[:n] = tokens.cpu()
+        static.update(handles)
+        tok_buf.copy_(host_tokens)
+        graph.replay()
+        replayed = logits[:n].float()
+        torch.cuda.synchronize()
+    eng.paged_cache.check_device_errors()
+    scale = eager.abs().max().item()
+    assert (replayed - eager).abs().max().item() <= 0.05 * scale
+    assert (replayed.argmax(-1) == eager.argmax(-1)).float().mean().item() >= 0.75
