@@ -161,7 +161,8 @@ class DecodeGraphs:
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
                 logits = packed_forward(model, tokens, static.batch, rows)
-        return graph, static, tokens, host_tokens, logits
+        # every tensor the graph reads must outlive it: rows is kept with the graph
+        return graph, static, tokens, host_tokens, logits, rows
 
     def step(self, decode) -> bool:
         """Run one decode tick for ``decode`` from a graph; False if no bucket fits."""
@@ -172,7 +173,7 @@ class DecodeGraphs:
         found = self._graph(n, max(h.length for h in handles) + 1)
         if found is None:
             return False
-        graph, static, tokens, host_tokens, logits = found
+        graph, static, tokens, host_tokens, logits, _ = found
         torch.cuda.current_stream().synchronize()  # the pinned token buffer is reused
         host_tokens.zero_()
         host_tokens[:n] = torch.tensor([request.tokens[-1] for request in decode])

@@ -149,7 +149,7 @@ def test_decode_graph_matches_eager_forward(model):
         batch = eng.paged_cache.begin_batch(handles, [1] * n)
         eager = packed_forward(model, tokens, batch, torch.arange(n, device="cuda")).float()
         graphs = DecodeGraphs(eng, sizes=(8,), kv_buckets=(2048,))
-        graph, static, tok_buf, host_tokens, logits = graphs._graph(n, max(h.length for h in handles) + 1)
+        graph, static, tok_buf, host_tokens, logits, _ = graphs._graph(n, max(h.length for h in handles) + 1)
         host_tokens.zero_()
         host_tokens[:n] = tokens.cpu()
         static.update(handles)
