@@ -829,4 +829,13 @@ int hyt_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
   return HYT_OK;
 }
 
+int hyt_wait_self_test(int32_t* error_word, int64_t* elapsed_ns, void* stream) {
+  g_last_error.clear();
+  if (error_word == nullptr || elapsed_ns == nullptr)
+    return fail(HYT_ERR_INVALID, "null error_word or elapsed_ns");
+  cudaError_t err = hyt::run_wait_self_test(error_word, elapsed_ns, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "wait self-test launch");
+  return HYT_OK;
+}
+
 }  // extern "C"

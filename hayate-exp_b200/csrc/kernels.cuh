@@ -145,4 +145,7 @@ struct NormRopeParams {
 };
 cudaError_t run_norm_rope_scatter(const NormRopeParams& p, int dtype, cudaStream_t stream);
 
+// Runs the bounded mbarrier wait into its time limit (see self_test.cu).
+cudaError_t run_wait_self_test(int32_t* error_word, int64_t* elapsed_ns, cudaStream_t stream);
+
 }  // namespace hyt

@@ -326,3 +326,20 @@ def read_device_errors(error_word: torch.Tensor) -> list[str]:
     """Decode (and synchronise on) a device error word; empty if no kernel refused anything."""
     value = int(error_word.item())
     return [msg for bit, msg in _lib.DEVICE_ERRORS.items() if value & bit]
+
+
+def wait_self_test(error_word: torch.Tensor) -> tuple[int, int]:
+    """Run the bounded-wait self-test (``hyt_wait_self_test``) on the current stream.
+
+    A wait on an mbarrier that nothing signals gives up after its 1 s limit and ORs the
+    wait-timeout bit into ``error_word``; a second wait of the same CTA then returns at
+    once. Returns both waits' durations in nanoseconds (synchronises).
+    """
+    _require_cuda(error_word)
+    if error_word.dtype != torch.int32 or error_word.numel() < 1:
+        raise ValueError("error_word must be a CUDA int32 tensor")
+    elapsed = torch.zeros(2, dtype=torch.int64, device=error_word.device)
+    rc = _lib.lib().hyt_wait_self_test(error_word.data_ptr(), elapsed.data_ptr(), _stream_ptr())
+    _lib.check(rc, "hyt_wait_self_test")
+    first, second = elapsed.tolist()
+    return first, second

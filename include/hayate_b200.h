@@ -244,6 +244,14 @@ size_t hyt_attention_workspace_bytes(int32_t batch, int32_t query_len, int32_t n
 /* Zero a workspace's counter area (enqueued on stream). */
 int hyt_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
 
+/* Self-test of the bounded pipeline wait (no hayate counterpart: hayate's PyTorch path
+ * has no device-side waits). One tiny kernel waits on an mbarrier that nothing signals;
+ * the wait gives up after its 1 s limit and ORs HYT_DEVERR_WAIT_TIMEOUT into
+ * *error_word, and a second wait of the same CTA returns at once through the CTA's
+ * abort flag. elapsed_ns (device, int64[2]) receives both waits' durations. No copy is
+ * in flight when the kernel exits, so the context stays usable. Takes about 1 s. */
+int hyt_wait_self_test(int32_t* error_word, int64_t* elapsed_ns, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
