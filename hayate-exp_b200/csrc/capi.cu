@@ -3,6 +3,7 @@
 // Host-side argument checks, TMA tensor maps over the KV pools, workspace
 // sizing and the choice between the decode, prefill and CUDA-core kernels.
 // Every entry point only enqueues work on the caller's stream.
+#include <algorithm>
 #include <mutex>
 #include <string>
 
@@ -120,6 +121,84 @@ int pool_tensor_map(const void* pool, int dtype, int head_dim, int64_t capacity,
   cache.used[slot] = true;
   *out = map;
   return HYT_OK;
+}
+
+// Tensor map over q for the prefill kernel's Q load: dims (head_dim, T, H, B), or
+// (head_dim, H, T, B) when the head stride is the smaller one (q viewed from a
+// [B, T, H, D] tensor), box [128 rows x 64 dims], 128-byte swizzle: the same shared-memory
+// layout as the K tiles. qs = {b, h, t} in elements (b unused when requests == 1).
+// Returns false, with nothing recorded as an error, when q cannot be described (the kernel
+// then loads Q with plain loads). Cached like the pool maps: the engine's q buffers come
+// back at the same addresses layer after layer.
+struct QMapKey {
+  const void* ptr;
+  int dtype, heads;
+  int64_t tokens, requests, sb, sh, st;
+  bool operator==(const QMapKey& o) const {
+    return ptr == o.ptr && dtype == o.dtype && heads == o.heads && tokens == o.tokens &&
+           requests == o.requests && sb == o.sb && sh == o.sh && st == o.st;
+  }
+};
+
+struct QMapCache {
+  static constexpr int kEntries = 64;
+  QMapKey keys[kEntries];
+  CUtensorMap maps[kEntries];
+  bool ht[kEntries];
+  bool used[kEntries] = {};
+  int next = 0;
+  std::mutex mu;
+};
+
+bool q_tensor_map(const void* q, const int64_t* qs, int dtype, int64_t tokens, int heads,
+                  int64_t requests, CUtensorMap* out, bool* ht_out) {
+  const int64_t eb = elem_bytes(dtype);
+  const int64_t sh = qs[1] * eb, st = qs[2] * eb;
+  if (reinterpret_cast<uintptr_t>(q) % 16 || sh <= 0 || st <= 0 || sh % 16 || st % 16 ||
+      tokens < 1 || heads < 1 || requests < 1)
+    return false;
+  int64_t sb = qs[0] * eb;
+  if (requests == 1) sb = std::max(sh * heads, st * tokens);  // any valid stride: one request
+  if (sb <= 0 || sb % 16) return false;
+  const int64_t kMaxStride = int64_t(1) << 40;
+  if (sh >= kMaxStride || st >= kMaxStride || sb >= kMaxStride || tokens >= (int64_t(1) << 31) ||
+      requests >= (int64_t(1) << 31))
+    return false;
+  static QMapCache cache;
+  const QMapKey key{q, dtype, heads, tokens, requests, sb, sh, st};
+  std::lock_guard<std::mutex> lock(cache.mu);
+  for (int i = 0; i < QMapCache::kEntries; ++i) {
+    if (cache.used[i] && cache.keys[i] == key) {
+      *out = cache.maps[i];
+      *ht_out = cache.ht[i];
+      return true;
+    }
+  }
+  EncodeTiledFn encode = encode_fn();
+  if (encode == nullptr) return false;
+  const bool ht = sh < st;
+  cuuint64_t dims[4] = {128, cuuint64_t(ht ? heads : tokens), cuuint64_t(ht ? tokens : heads),
+                        cuuint64_t(requests)};
+  cuuint64_t strides[3] = {cuuint64_t(ht ? sh : st), cuuint64_t(ht ? st : sh), cuuint64_t(sb)};
+  cuuint32_t box[4] = {64, ht ? 1u : 128u, ht ? 128u : 1u, 1};
+  cuuint32_t estrides[4] = {1, 1, 1, 1};
+  CUtensorMap map;
+  CUresult res = encode(&map,
+                        dtype == HYT_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                               : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                        4, const_cast<void*>(q), dims, strides, box, estrides,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (res != CUDA_SUCCESS) return false;
+  const int slot = cache.next;
+  cache.next = (cache.next + 1) % QMapCache::kEntries;
+  cache.keys[slot] = key;
+  cache.maps[slot] = map;
+  cache.ht[slot] = ht;
+  cache.used[slot] = true;
+  *out = map;
+  *ht_out = ht;
+  return true;
 }
 
 // ------------------------------------------------------------------ argument checks
@@ -329,7 +408,13 @@ int launch_prefill(const void* q, const int64_t* qs, const void* k_pool, const v
   hyt::AttentionParams p = attention_params(q, qs, k_pool, v_pool, g, page_table, cache_lens,
                                             out, os, scale, error_word);
   apply_packed(p, pk);
-  cudaError_t err = hyt::run_prefill_attention(p, k_map, v_map, g.dtype, stream);
+  CUtensorMap q_map;
+  bool q_ht = false;
+  const bool packed = pk != nullptr;
+  const bool q_tma = q_tensor_map(q, qs, g.dtype, packed ? pk->total_tokens : g.query_len,
+                                  g.num_q_heads, packed ? 1 : g.batch, &q_map, &q_ht);
+  cudaError_t err = hyt::run_prefill_attention(p, k_map, v_map, q_tma ? &q_map : nullptr, q_ht,
+                                               g.dtype, stream);
   if (err != cudaSuccess) return cuda_fail(err, "prefill attention launch");
   return HYT_OK;
 }

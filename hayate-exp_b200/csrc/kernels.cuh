@@ -109,8 +109,12 @@ cudaError_t run_decode_attention(const AttentionParams& p, const DecodeLaunch& d
 
 // ------------------------------------------------------------ (b) tcgen05 chunked prefill
 // bf16/f16, head_dim 128, page_size % 128 == 0, q/out rows 16-byte aligned.
+// q_map (optional): a 4-D tensor map over q, dims (head_dim, T, H_q, B) or, with q_ht,
+// (head_dim, H_q, T, B), box 64 x 128 rows, 128-byte swizzle; T is query_len (the token
+// axis for packed batches, B = 1). Without it the softmax warps load Q themselves.
 cudaError_t run_prefill_attention(const AttentionParams& p, const CUtensorMap& k_map,
-                                  const CUtensorMap& v_map, int dtype, cudaStream_t stream);
+                                  const CUtensorMap& v_map, const CUtensorMap* q_map, bool q_ht,
+                                  int dtype, cudaStream_t stream);
 
 // ------------------------------------------------------------ fused QK-norm + RoPE + scatter
 struct NormRopeParams {

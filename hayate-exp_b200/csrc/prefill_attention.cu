@@ -20,11 +20,12 @@
 //     both) and writes P as packed bf16/f16 back over its S columns (tcgen05.st).
 //     At the end the pair adds its row sums and each warp normalises its half of the
 //     O rows, stages them in shared memory (the idle K/V stages) and stores them with
-//     coalesced 128-byte row segments. Q comes in the same way: one warp load covers
-//     two whole rows.
-//   warp 16 (producer): per 128-key tile looks the page up and TMA-loads K and V
-//     (2 boxes of [128 tokens x 64 dims] each, 128B swizzle) into 2-stage rings,
-//     prefetching the tile kPrefetchTiles ahead into L2.
+//     coalesced 128-byte row segments.
+//   warp 16 (producer): first TMA-loads Q_A and Q_B (through a tensor map over q; when
+//     q has none, the softmax warps load Q with one warp load per two whole rows), then
+//     per 128-key tile looks the page up, checks it, and TMA-loads K and V (2 boxes of
+//     [128 tokens x 64 dims] each, 128B swizzle) into 2-stage rings, prefetching the
+//     tile kPrefetchTiles ahead into L2.
 //   warp 17 (MMA issuer): S_x = Q_x K^T (M=128, N=128, 8 x K=16) and O_x += P_x V with
 //     P read straight from TMEM (tcgen05.mma, A in TMEM) and V as an MN-major
 //     shared-memory operand. The whole warp walks the loop and waits on the barriers;
@@ -80,6 +81,8 @@ constexpr int kPrefetchTiles = 3;          // L2 prefetch distance of the K/V st
 struct PrefillKernelParams {
   AttentionParams a;
   int32_t group;
+  int32_t q_tma;  // Q arrives by TMA through q_map (else the softmax warps load it)
+  int32_t q_ht;   // q_map's dims are (d, head, token, request), else (d, token, head, request)
 };
 
 // Byte offset of 16-byte chunk `chunk` (0..15) of row `r` in a [128 x 128] tile
@@ -125,8 +128,10 @@ struct Barriers {
   uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
   uint64_t s_full[2], p_full[2];  // per tile (A, B)
   uint64_t o_done, drain;
+  uint64_t prod_done;  // the producer has issued its last load (and set `bad`)
   uint32_t tmem_base;
   int32_t abort;  // set once a bounded wait gave up: later waits return at once
+  int32_t bad;    // device error bits of a refused page table: the CTA writes zeros
 };
 static_assert(sizeof(Barriers) <= 256, "barrier block");
 
@@ -135,6 +140,7 @@ template <typename T, bool kPacked>
 __global__ void __maxnreg__(96)
     prefill_attention_kernel(const __grid_constant__ CUtensorMap k_map,
                              const __grid_constant__ CUtensorMap v_map,
+                             const __grid_constant__ CUtensorMap q_map,
                              const PrefillKernelParams P) {
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   const AttentionParams& p = P.a;
@@ -171,22 +177,12 @@ __global__ void __maxnreg__(96)
   const int32_t* table = p.page_table + int64_t(b) * p.page_table_stride;
   const int page_mask = (1 << p.page_shift) - 1;
 
-  // ---- refuse page ids that would address outside the pool (before any load)
-  int bad = cache_len < 0 ? HYT_DEVERR_TABLE_RANGE : 0;
-  if (p.error_word != nullptr && (*reinterpret_cast<volatile int32_t*>(p.error_word) & HYT_DEVERR_WAIT_TIMEOUT))
-    bad |= HYT_DEVERR_WAIT_TIMEOUT;  // an earlier CTA's wait gave up: start no pipeline
-  for (int j = threadIdx.x; j < n_tiles && !bad; j += kThreads) {
-    const int lp = (j * kKeys) >> p.page_shift;
-    if (lp >= p.page_table_stride) {
-      bad |= HYT_DEVERR_TABLE_RANGE;
-    } else {
-      const int32_t page = table[lp];
-      if (page < 0 || page >= p.num_pages) bad |= HYT_DEVERR_PAGE_RANGE;
-    }
-  }
-  bad = __syncthreads_or(bad);
-  if (bad) {
-    if (threadIdx.x == 0) flag_error(p.error_word, bad);
+  // ---- a negative cache length, or one that needs more pages than the table row holds,
+  // refuses the CTA before any load (arithmetic only). Page ids are checked by the
+  // producer as it reaches each tile (off the start-up path); a refused tile is not
+  // loaded and the CTA writes zeros.
+  if (cache_len < 0 || ((int64_t(n_tiles - 1) * kKeys) >> p.page_shift) >= p.page_table_stride) {
+    if (threadIdx.x == 0) flag_error(p.error_word, HYT_DEVERR_TABLE_RANGE);
     for (int idx = threadIdx.x; idx < 2 * kRows * kD; idx += kThreads) {
       const int x = idx / (kRows * kD), r = (idx / kD) % kRows, d = idx % kD;
       if (t0 + r < query_len) {
@@ -199,7 +195,8 @@ __global__ void __maxnreg__(96)
 
   if (threadIdx.x == 0) {
     bars->abort = 0;
-    mbar_init(&bars->q_full, kSoftmaxThreads);
+    bars->bad = 0;
+    mbar_init(&bars->q_full, P.q_tma ? 1 : kSoftmaxThreads);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->k_empty[s], 1);
@@ -210,6 +207,7 @@ __global__ void __maxnreg__(96)
     }
     mbar_init(&bars->o_done, 1);
     mbar_init(&bars->drain, 1);
+    mbar_init(&bars->prod_done, 1);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -227,15 +225,42 @@ __global__ void __maxnreg__(96)
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
+      if (P.q_tma) {  // Q first: the first QK waits for it and for K tile 0
+        const int q_row0 = kPacked ? p.q_start[b] + t0 : t0;
+        const int q_req = kPacked ? 0 : b;
+        mbar_arrive_expect_tx(&bars->q_full, 2 * kTileBytes);
+#pragma unroll
+        for (int qx = 0; qx < 2; ++qx)
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint8_t* dst = smem + kQOff + qx * kTileBytes + c * kChunkBytes;
+            if (P.q_ht)
+              tma_load_4d(dst, &q_map, &bars->q_full, c * 64, h0 + qx, q_row0, q_req);
+            else
+              tma_load_4d(dst, &q_map, &bars->q_full, c * 64, q_row0, h0 + qx, q_req);
+          }
+      }
       tma_prefetch_desc(&k_map);
       tma_prefetch_desc(&v_map);
       const int plane = p.layer * p.num_kv_heads + g;
-      auto tile_row = [&](int j) {
+      // an earlier CTA's wait gave up: load nothing (the CTA writes zeros)
+      int bad = (err != nullptr && (*reinterpret_cast<volatile int32_t*>(err) & HYT_DEVERR_WAIT_TIMEOUT))
+                    ? HYT_DEVERR_WAIT_TIMEOUT : 0;
+      // pool row of key tile j, or -1 (and the error bit in `why`) for a page id outside
+      // the pool; the table row is long enough for every tile (checked above)
+      auto tile_row = [&](int j, int& why) {
         const int tok = j * kKeys;
-        return (table[tok >> p.page_shift] << p.page_shift) + (tok & page_mask);
+        const int32_t page = table[tok >> p.page_shift];
+        if (page < 0 || page >= p.num_pages) {
+          why |= HYT_DEVERR_PAGE_RANGE;
+          return -1;
+        }
+        return (page << p.page_shift) + (tok & page_mask);
       };
       auto prefetch = [&](int j) {  // K and V of tile j into L2
-        const int row = tile_row(j);
+        int why = 0;
+        const int row = tile_row(j, why);
+        if (why) return;  // refused when its turn to load comes
         tma_prefetch_l2_3d(&k_map, 0, row, plane);
         tma_prefetch_l2_3d(&k_map, 64, row, plane);
         tma_prefetch_l2_3d(&v_map, 0, row, plane);
@@ -244,27 +269,42 @@ __global__ void __maxnreg__(96)
       // Tiles 0 and 1 are loaded at once (both ring stages are free); from iteration 1 on,
       // each iteration prefetches into L2 the tile kPrefetchTiles beyond the one it loads.
       // No prefetch burst at start-up: the whole first wave loads Q and its first tiles
-      // then, sharing HBM.
+      // then, sharing HBM. Once a page id is refused, later stages are released without a
+      // load (plain arrivals) so every role still walks the same number of tiles.
       for (int j = 0; j < n_tiles; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
-        if (j >= 1 && j + kPrefetchTiles < n_tiles) prefetch(j + kPrefetchTiles);
-        const int row = tile_row(j);
+        if (!bad && j >= 1 && j + kPrefetchTiles < n_tiles) prefetch(j + kPrefetchTiles);
+        const int row = bad ? -1 : tile_row(j, bad);
         if (j >= 2) mbar_wait(&bars->k_empty[st], ph ^ 1, err, abort);
         uint8_t* kdst = smem + kKOff + st * kTileBytes;
-        mbar_arrive_expect_tx(&bars->k_full[st], kTileBytes);
-        tma_load_3d(kdst, &k_map, &bars->k_full[st], 0, row, plane);
-        tma_load_3d(kdst + kChunkBytes, &k_map, &bars->k_full[st], 64, row, plane);
+        if (!bad) {
+          mbar_arrive_expect_tx(&bars->k_full[st], kTileBytes);
+          tma_load_3d(kdst, &k_map, &bars->k_full[st], 0, row, plane);
+          tma_load_3d(kdst + kChunkBytes, &k_map, &bars->k_full[st], 64, row, plane);
+        } else {
+          mbar_arrive(&bars->k_full[st]);
+        }
         if (j >= 2) mbar_wait(&bars->v_empty[st], ph ^ 1, err, abort);
         uint8_t* vdst = smem + kVOff + st * kTileBytes;
-        mbar_arrive_expect_tx(&bars->v_full[st], kTileBytes);
-        tma_load_3d(vdst, &v_map, &bars->v_full[st], 0, row, plane);
-        tma_load_3d(vdst + kChunkBytes, &v_map, &bars->v_full[st], 64, row, plane);
+        if (!bad) {
+          mbar_arrive_expect_tx(&bars->v_full[st], kTileBytes);
+          tma_load_3d(vdst, &v_map, &bars->v_full[st], 0, row, plane);
+          tma_load_3d(vdst + kChunkBytes, &v_map, &bars->v_full[st], 64, row, plane);
+        } else {
+          mbar_arrive(&bars->v_full[st]);
+        }
       }
+      if (bad) {
+        flag_error(err, bad);
+        bars->bad = bad;
+      }
+      mbar_arrive(&bars->prod_done);  // release: `bad` is visible to whoever waits on it
       for (int j = max(0, n_tiles - 2); j < n_tiles; ++j) {  // nothing in flight at exit
         mbar_drain(&bars->k_full[j & 1], (j >> 1) & 1);
         mbar_drain(&bars->v_full[j & 1], (j >> 1) & 1);
       }
+      if (P.q_tma) mbar_drain(&bars->q_full, 0);
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
@@ -358,9 +398,10 @@ __global__ void __maxnreg__(96)
     float* red_max = reinterpret_cast<float*>(smem + kRedOff) + x * (2 * 2 * kRows);  // [parity][half][row]
     float* red_sum = reinterpret_cast<float*>(smem + kRedOff) + 2 * (2 * 2 * kRows) + x * (2 * kRows);
 
-    {  // Q rows -> swizzled shared memory; one warp load covers 2 whole rows (512 B). All
-       // eight loads are issued before the first shared store (one memory round trip, not
-       // eight: the stores would otherwise be ordered behind each load).
+    if (!P.q_tma) {  // Q rows -> swizzled shared memory (when q has no tensor map); one
+       // warp load covers 2 whole rows (512 B). All eight loads are issued before the first
+       // shared store (one memory round trip, not eight: the stores would otherwise be
+       // ordered behind each load).
       uint4 v[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -449,10 +490,13 @@ __global__ void __maxnreg__(96)
     // 128-byte row segments instead of 16 bytes of 32 different rows.
     red_sum[half * kRows + r] = l_run;
     mbar_wait(&bars->o_done, 0, err, abort);
+    mbar_wait(&bars->prod_done, 0, err, abort);
     tc_fence_after();
     named_bar_sync(pair_bar, 64);
     const float l = red_sum[r] + red_sum[kRows + r];
     const float inv = l > 0.f ? 1.f / l : 0.f;
+    // a refused page table: zeros (`bad` is published by the producer's prod_done arrival)
+    const bool refused = *reinterpret_cast<volatile int32_t*>(&bars->bad) != 0;
     uint8_t* stage = smem + kKOff + x * kRows * kStageRowBytes + half * 128;
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
@@ -466,6 +510,7 @@ __global__ void __maxnreg__(96)
         w.y = Elem<T>::pack2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
         w.z = Elem<T>::pack2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
         w.w = Elem<T>::pack2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+        if (refused) w = make_uint4(0u, 0u, 0u, 0u);
         *reinterpret_cast<uint4*>(stage + r * kStageRowBytes + (c * 4 + v) * 16) = w;
       }
     }
@@ -491,16 +536,19 @@ __global__ void __maxnreg__(96)
 }  // namespace
 
 cudaError_t run_prefill_attention(const AttentionParams& p, const CUtensorMap& k_map,
-                                  const CUtensorMap& v_map, int dtype, cudaStream_t stream) {
+                                  const CUtensorMap& v_map, const CUtensorMap* q_map, bool q_ht,
+                                  int dtype, cudaStream_t stream) {
   PrefillKernelParams P;
   P.a = p;
   P.group = p.num_q_heads / p.num_kv_heads;
+  P.q_tma = q_map != nullptr ? 1 : 0;
+  P.q_ht = q_ht ? 1 : 0;
   const dim3 grid(unsigned((p.query_len + kRows - 1) / kRows), unsigned(p.num_q_heads / 2),
                   unsigned(att_launch_count(p)));
   auto launch = [&](auto kernel) {
     cudaError_t e = allow_smem(kernel, kSmemBytes, stream);
     if (e != cudaSuccess) return e;
-    kernel<<<grid, kThreads, kSmemBytes, stream>>>(k_map, v_map, P);
+    kernel<<<grid, kThreads, kSmemBytes, stream>>>(k_map, v_map, q_map != nullptr ? *q_map : k_map, P);
     return cudaSuccess;
   };
   const bool packed = p.q_start != nullptr;

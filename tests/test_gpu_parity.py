@@ -252,16 +252,60 @@ def test_full_size_prefill_config():
     assert err <= 2e-2, err
 
 
-def test_prefill_flags_bad_page_ids():
+@pytest.mark.parametrize("column", [0, 1, 2])
+def test_prefill_flags_bad_page_ids(column):
+    """A page id outside the pool, in the first, a middle or the last key tile: refused by
+    the producer when it reaches that tile; the CTA writes zeros and the next call is clean."""
     manager, _, batch, q, k, v = build_step([300], 40, seed=2)
+    batch.write_layer(0, k, v)
     table = batch.page_table.clone()
-    table[0, 1] = -7
+    table[0, column] = -7 if column != 1 else manager.num_pages
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     out = ops.paged_attention(q, manager.k_cache, manager.v_cache, 0, table, batch.cache_lens_i32,
                               manager.page_size, 340, error_word=err, kernel="prefill")
     torch.cuda.synchronize()
-    assert int(err.item()) & 1
+    assert ops.read_device_errors(err) == ["page id outside the pool"]
     assert float(out.float().abs().max()) == 0.0  # refused CTAs write zeros
+    err.zero_()
+    good = ops.paged_attention(q, manager.k_cache, manager.v_cache, 0, batch.page_table,
+                               batch.cache_lens_i32, manager.page_size, 340, error_word=err,
+                               kernel="prefill")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert np.abs(good.float().cpu().numpy() - oracle_out(manager, batch, q)).max() <= 2e-2
+
+
+def test_prefill_flags_short_page_table():
+    """A table row with fewer pages than the kv length needs is refused before any load."""
+    manager, _, batch, q, k, v = build_step([300], 40, seed=3)
+    table = batch.page_table[:, :2].contiguous()  # 340 keys need 3 pages of 128
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = ops.paged_attention(q, manager.k_cache, manager.v_cache, 0, table, batch.cache_lens_i32,
+                              manager.page_size, 340, error_word=err, kernel="prefill")
+    torch.cuda.synchronize()
+    assert ops.read_device_errors(err) == ["kv length needs more pages than the page table row holds"]
+    assert float(out.float().abs().max()) == 0.0
+
+
+def test_prefill_q_load_paths_agree():
+    """Q by TMA (q in [B, H, T, D] or [B, T, H, D] memory) and Q by plain loads (a q
+    broadcast over the batch, which no tensor map describes) give identical rows."""
+    manager, _, batch, q, k, v = build_step([0, 700, 129], 300, seed=8)
+    batch.write_layer(0, k, v)
+    one = q[:1]
+    broadcast = one.expand(3, -1, -1, -1)                         # b stride 0: plain loads
+    contiguous = broadcast.contiguous()                           # (d, t, h, b) map
+    transposed = broadcast.transpose(1, 2).contiguous().transpose(1, 2)  # (d, h, t, b) map
+    outs = []
+    for qq in (broadcast, contiguous, transposed):
+        outs.append(ops.paged_attention(qq, manager.k_cache, manager.v_cache, 0, batch.page_table,
+                                        batch.cache_lens_i32, manager.page_size, batch.max_kv_len,
+                                        error_word=manager.error_word, kernel="prefill"))
+    torch.cuda.synchronize()
+    manager.check_device_errors()
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    err = np.abs(outs[1].float().cpu().numpy() - oracle_out(manager, batch, contiguous)).max()
+    assert err <= 2e-2, err
 
 
 def reference_norm_rope(x: torch.Tensor, weight: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
