@@ -278,7 +278,8 @@ def test_prefill_flags_bad_page_ids(column):
 def test_prefill_flags_short_page_table():
     """A table row with fewer pages than the kv length needs is refused before any load."""
     manager, _, batch, q, k, v = build_step([300], 40, seed=3)
-    table = batch.page_table[:, :2].contiguous()  # 340 keys need 3 pages of 128
+    table = torch.empty((1, 2), dtype=torch.int32, device="cuda")  # row stride 2: 2 pages,
+    table.copy_(batch.page_table[:, :2])                            # 340 keys need 3
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     out = ops.paged_attention(q, manager.k_cache, manager.v_cache, 0, table, batch.cache_lens_i32,
                               manager.page_size, 340, error_word=err, kernel="prefill")
