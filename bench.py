@@ -86,7 +86,7 @@ def decode_lengths(seed: int, batch: int = 64, lo: int = 1024, hi: int = 8192):
 # from one ncu capture each: config 2 decode scaled from a 16-request capture by kv tokens
 # (1.028 x the algorithmic bytes), config 3 prefill captured at full size.
 DECODE_CFG2_TRAFFIC = 1.217e9
-PREFILL_CFG3_TRAFFIC = 144.89e6
+PREFILL_CFG3_TRAFFIC = 145.36e6
 
 
 def attention_flops(cache_lens, query_len: int, num_q_heads: int, head_dim: int) -> int:
