@@ -20,7 +20,11 @@
 
 namespace hyt {
 
-template <int kElemBytes, int kVecBytes>
+// One VEC-byte chunk per thread. The source chunk is loaded first: its address depends
+// only on the thread's (row, chunk), so the load overlaps the dependent cache-length ->
+// page-table lookups that give the destination. Index arithmetic runs in Index (32-bit
+// whenever the launch's chunk count fits, the common case).
+template <int kElemBytes, int kVecBytes, typename Index>
 __global__ void __launch_bounds__(256) kv_scatter_kernel(const ScatterParams p) {
   using Vec = typename std::conditional<
       kVecBytes == 16, uint4,
@@ -28,37 +32,42 @@ __global__ void __launch_bounds__(256) kv_scatter_kernel(const ScatterParams p) 
                                 typename std::conditional<kVecBytes == 4, uint32_t,
                                                           uint16_t>::type>::type>::type;
   constexpr int kVecElems = kVecBytes / kElemBytes;
-  const int chunks = p.head_dim / kVecElems;
+  const Index chunks = Index(p.head_dim / kVecElems);
   const bool packed = p.token_request != nullptr;
-  const int64_t rows = (packed ? int64_t(p.total_tokens) : int64_t(p.batch) * p.query_len) * p.heads;
-  const int64_t total = 2 * rows * chunks;
+  const Index rows = Index(packed ? int64_t(p.total_tokens) : int64_t(p.batch) * p.query_len) * Index(p.heads);
+  const Index total = 2 * rows * chunks;
   const int32_t page_mask = (1 << p.page_shift) - 1;
-  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total;
-       i += int64_t(gridDim.x) * blockDim.x) {
-    const int chunk = int(i % chunks);
-    int64_t row = i / chunks;
+  for (Index i = Index(blockIdx.x) * Index(blockDim.x) + Index(threadIdx.x); i < total;
+       i += Index(gridDim.x) * Index(blockDim.x)) {
+    const Index chunk = i % chunks;
+    Index row = i / chunks;
     const bool is_v = row >= rows;
     if (is_v) row -= rows;
-    const int h = int(row % p.heads);
+    const Index h = row % Index(p.heads);
+    const Index tok = row / Index(p.heads);  // packed: token index; else b * query_len + t
     int t, b;
     int64_t token_elem;  // element offset of this token's row (head offset not included)
     if (packed) {
-      const int64_t tok = row / p.heads;
+      token_elem = int64_t(tok) * (is_v ? p.v_st : p.k_st);
+    } else {
+      t = int(tok % Index(p.query_len));
+      b = int(tok / Index(p.query_len));
+      token_elem = is_v ? (b * p.v_sb + t * p.v_st) : (b * p.k_sb + t * p.k_st);
+    }
+    const int64_t src_elem = token_elem + int64_t(h) * (is_v ? p.v_sh : p.k_sh);
+    const Vec v = *reinterpret_cast<const Vec*>((is_v ? p.v_new : p.k_new) +
+                                                (src_elem + int64_t(chunk) * kVecElems) * kElemBytes);
+    if (packed) {
       b = p.token_request[tok];
       if (b < 0 || b >= p.batch) {
         flag_error(p.error_word, HYT_DEVERR_PACKED_RANGE);
         continue;
       }
-      t = int(tok - p.q_start[b]);
+      t = int(int64_t(tok) - p.q_start[b]);
       if (t < 0) {
         flag_error(p.error_word, HYT_DEVERR_PACKED_RANGE);
         continue;
       }
-      token_elem = tok * (is_v ? p.v_st : p.k_st);
-    } else {
-      t = int((row / p.heads) % p.query_len);
-      b = int(row / (int64_t(p.heads) * p.query_len));
-      token_elem = is_v ? (b * p.v_sb + t * p.v_st) : (b * p.k_sb + t * p.k_st);
     }
     const int64_t pos = int64_t(p.cache_lens[b]) + t;
     const int64_t logical_page = pos >> p.page_shift;
@@ -72,11 +81,9 @@ __global__ void __launch_bounds__(256) kv_scatter_kernel(const ScatterParams p) 
       continue;
     }
     const int64_t slot = (int64_t(page) << p.page_shift) + (pos & page_mask);
-    const int64_t src_elem = token_elem + h * (is_v ? p.v_sh : p.k_sh);
-    const int64_t dst_elem = p.layer_offset + (h * p.capacity + slot) * p.head_dim;
-    const uint8_t* src = (is_v ? p.v_new : p.k_new) + (src_elem + int64_t(chunk) * kVecElems) * kElemBytes;
+    const int64_t dst_elem = p.layer_offset + (int64_t(h) * p.capacity + slot) * p.head_dim;
     uint8_t* dst = (is_v ? p.v_pool : p.k_pool) + (dst_elem + int64_t(chunk) * kVecElems) * kElemBytes;
-    *reinterpret_cast<Vec*>(dst) = *reinterpret_cast<const Vec*>(src);
+    *reinterpret_cast<Vec*>(dst) = v;
   }
 }
 
@@ -86,10 +93,17 @@ static cudaError_t launch_scatter(const ScatterParams& p, cudaStream_t stream) {
   const int64_t tokens = p.token_request != nullptr ? int64_t(p.total_tokens) : int64_t(p.batch) * p.query_len;
   const int64_t total = 2 * tokens * p.heads * (p.head_dim / kVecElems);
   const int threads = 256;
+  // one chunk per thread (a single pass: each thread's dependent lookups are paid once);
+  // grid-stride only beyond 64 resident-size waves. Four chunks per thread with all
+  // source loads first measured slower at decode sizes (fewer threads) and equal at
+  // prefill sizes.
   int64_t blocks = (total + threads - 1) / threads;
-  if (blocks > 148 * 16) blocks = 148 * 16;  // grid-stride beyond 16 blocks per SM
+  if (blocks > 148 * 8 * 64) blocks = 148 * 8 * 64;
   if (blocks < 1) blocks = 1;
-  kv_scatter_kernel<kElemBytes, kVecBytes><<<int(blocks), threads, 0, stream>>>(p);
+  if (total + int64_t(blocks) * threads < (int64_t(1) << 31))
+    kv_scatter_kernel<kElemBytes, kVecBytes, int32_t><<<int(blocks), threads, 0, stream>>>(p);
+  else
+    kv_scatter_kernel<kElemBytes, kVecBytes, int64_t><<<int(blocks), threads, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
