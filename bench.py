@@ -247,7 +247,20 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
     out = torch.empty((len(ctx), 1, 32, 128), dtype=q.dtype, device="cuda").transpose(1, 2)
     ws = manager.workspace_for(len(ctx), 1, 32, batch.max_kv_len)
 
-    def step(attn_events=None):
+    def step(events=None):
+        """One decode step: the new K/V rows are written and attended by one launch of the
+        decode kernel (PagedKVBatch.write_attend_layer's path)."""
+        if events is not None:
+            events[0].record()
+        ops.paged_attention_scatter(q, k, v, manager.k_cache, manager.v_cache, 0, batch.page_table,
+                                    batch.cache_lens_i32, 128, batch.max_kv_len, out=out,
+                                    workspace=ws, error_word=manager.error_word,
+                                    split_tokens=args.split_tokens)
+        if events is not None:
+            events[1].record()
+
+    def unfused_step(attn_events=None):
+        """The same step as two launches: the scatter kernel, then the decode kernel."""
         ops.kv_scatter(k, v, manager.k_cache, manager.v_cache, 0, batch.page_table,
                        batch.cache_lens_i32, 128, error_word=manager.error_word)
         if attn_events is not None:
@@ -260,10 +273,11 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
 
     for _ in range(args.warmup):
         step()
+        unfused_step()
     torch.cuda.synchronize()
     manager.check_device_errors()
 
-    attn = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+    kern = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
@@ -271,18 +285,36 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
         torch.cuda.synchronize()
         start.record()
         for i in range(args.steps):
-            step(attn[i])
+            step(kern[i])
         end.record()
         torch.cuda.synchronize()
         barrier(world)
     ms_local = start.elapsed_time(end)
-    attn_ms = sum(a.elapsed_time(b) for a, b in attn) / args.steps
+    kernel_ms = sum(a.elapsed_time(b) for a, b in kern) / args.steps
     manager.check_device_errors()
     ms_total = max_over_ranks(ms_local, world)
     total_bytes = sum_over_ranks(float(step_bytes), world)
     value = total_bytes * args.steps / (ms_total / 1e3) / 1e9
-    achieved = kv_bytes / (attn_ms / 1e3) / 1e9
+    achieved = step_bytes / (kernel_ms / 1e3) / 1e9
     peak = peaks["hbm_gbs"]
+
+    # the two-launch step beside it (outside the timed region): scatter, then attention alone
+    n_unfused = max(1, args.steps // 4)
+    attn = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            for _ in range(n_unfused)]
+    u0, u1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    u0.record()
+    for i in range(n_unfused):
+        unfused_step(attn[i])
+    u1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    unfused_ms = max_over_ranks(u0.elapsed_time(u1), world) / n_unfused
+    attn_ms = sum(a.elapsed_time(b) for a, b in attn) / n_unfused
+    attn_gbs = kv_bytes / (attn_ms / 1e3) / 1e9
+    manager.check_device_errors()
 
     result = {
         "metric": "decode attn HBM GB/s (% of peak)",
@@ -298,7 +330,7 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
         "dtype": "bf16",
         "data": "synthetic: seeded N(0,1) q/k/v, QK-norm + RoPE theta 1e6 at true positions, shuffled page tables",
         "config": {
-            "workload": "config 2: bf16 paged decode sweep (scatter + split-KV decode attention, 1 layer)",
+            "workload": "config 2: bf16 paged decode sweep (scatter + split-KV decode attention, 1 layer; the decode kernel writes the new K/V rows itself)",
             "requests_per_gpu": len(ctx), "kv_len": "U[1024, 8192]", "mean_kv_len": round(float(np.mean(ctx)), 1),
             "query_heads": 32, "kv_heads": 8, "head_dim": 128, "page_size": 128,
             "l2": "inputs larger than L2 (KV read per step ~%.2f GB > 126 MB)" % (kv_bytes / 1e9),
@@ -306,15 +338,18 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
             "split_tokens": args.split_tokens or "auto",
         },
         "step_bytes_per_gpu": step_bytes,
-        "attention_only": {"ms": round(attn_ms, 4), "GB_s": round(achieved, 1),
-                           "frac_of_peak": round(achieved / peak, 4)},
+        "unfused": {"step_ms": round(unfused_ms, 4), "step_GB_s": round(step_bytes / (unfused_ms / 1e3) / 1e9, 1),
+                    "attention_ms": round(attn_ms, 4), "attention_GB_s": round(attn_gbs, 1),
+                    "attention_frac_of_peak": round(attn_gbs / peak, 4),
+                    "what": "kv_scatter launch + decode launch (no fused rows), same inputs, %d steps" % n_unfused},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
                      "nominal_frac_8TBs": round(achieved / 8000.0, 4),
                      "traffic": DECODE_CFG2_TRAFFIC if len(ctx) == 64 else None,
                      "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + write.sum)",
-                     "kernel": "decode_attention_kernel (split-KV decode)"},
-        "gpu_launches": 2 * args.steps,
+                     "bytes_per_launch": step_bytes,
+                     "kernel": "decode_attention_kernel (split-KV decode with the fused row scatter)"},
+        "gpu_launches": args.steps,
         "clocks": clocks.summary(),
     }
     if args.reference_gpu and rank == 0:
@@ -354,8 +389,7 @@ def decode_e2e(args, world, manager, handles, ctx, q, k, v, step_bytes):
         qd = q_h.to("cuda", non_blocking=True)
         kd = k_h.to("cuda", non_blocking=True)
         vd = v_h.to("cuda", non_blocking=True)
-        batch.write_layer(0, kd, vd)
-        o = batch.attend_layer(qd, 0)
+        o = batch.write_attend_layer(0, kd, vd, qd)
         out_h[0].copy_(o, non_blocking=True)                  # D2H of the step's result
 
     compute = torch.cuda.current_stream()
@@ -383,8 +417,7 @@ def decode_e2e(args, world, manager, handles, ctx, q, k, v, step_bytes):
             compute.wait_event(inputs_ready[s])
             batch = manager.begin_batch(handles, 1)
             qd, kd, vd = dev[s]
-            batch.write_layer(0, kd, vd)
-            o = batch.attend_layer(qd, 0)
+            o = batch.write_attend_layer(0, kd, vd, qd)
             inputs_free[s].record(compute)
             output_ready[s].record(compute)
             with torch.cuda.stream(copier):
@@ -416,8 +449,9 @@ def decode_e2e(args, world, manager, handles, ctx, q, k, v, step_bytes):
                        "ms_per_step": round(ms_serial / args.steps, 4)},
             "h2d_bytes_per_step": int(q_h.numel() * 2 + k_h.numel() * 2 + v_h.numel() * 2 + meta_bytes),
             "d2h_bytes_per_step": int(out_h[0].numel() * 2),
-            "path": "PagedKVCacheManager.begin_batch -> write_layer -> attend_layer, pinned host "
-                    "buffers; copies on a second stream overlap the neighbouring steps"}
+            "path": "PagedKVCacheManager.begin_batch -> PagedKVBatch.write_attend_layer (write_layer + "
+                    "attend_layer in one launch), pinned host buffers; copies on a second stream "
+                    "overlap the neighbouring steps"}
 
 
 def cpu_threads() -> int:
@@ -577,10 +611,9 @@ def run_longdecode(args, world, rank, local, peaks, peak_kind):
     def step(s, ev=None):
         batch = manager.begin_batch(handles, 1)
         q, k, v = inputs[s]
-        batch.write_layer(0, k, v)
         if ev is not None:
             ev[0].record()
-        batch.attend_layer(q, 0)
+        batch.write_attend_layer(0, k, v, q)  # one launch: the decode kernel writes the rows
         if ev is not None:
             ev[1].record()
         manager.commit_batch(handles, 1)
@@ -626,7 +659,7 @@ def run_longdecode(args, world, rank, local, peaks, peak_kind):
                      "logical_GB_s": round(logical_per_step / (attn_ms / 1e3) / 1e9, 1), "traffic": None,
                      "kernel": "decode_attention_kernel"},
         "attention_ms_per_step": round(attn_ms, 4),
-        "gpu_launches": 2 * steps,
+        "gpu_launches": steps,
         "clocks": clocks.summary(),
     }
 

@@ -343,11 +343,19 @@ DecodeLayout decode_layout(int32_t batch, int32_t query_len, int32_t num_q_heads
   return L;
 }
 
+// The step's new K/V rows for a decode launch that writes them itself (fused scatter).
+struct FusedScatter {
+  const void* k_new;
+  const void* v_new;
+  const int64_t* strides;  // {k_b, k_h, k_t, v_b, v_h, v_t} in elements
+};
+
 int launch_decode(const void* q, const int64_t* qs, const void* k_pool, const void* v_pool,
                   const Geometry& g, const int32_t* page_table, const int32_t* cache_lens,
                   void* out, const int64_t* os, float scale, int32_t max_kv_len,
                   int32_t split_tokens, void* workspace, size_t workspace_bytes,
-                  int32_t* error_word, cudaStream_t stream, const PackedArgs* pk = nullptr) {
+                  int32_t* error_word, cudaStream_t stream, const PackedArgs* pk = nullptr,
+                  const FusedScatter* fs = nullptr) {
   if (max_kv_len < g.query_len) return fail(HYT_ERR_INVALID, "max_kv_len must be >= query_len");
   if (split_tokens < 0) return fail(HYT_ERR_INVALID, "split_tokens must be >= 0");
   const int32_t count = pk != nullptr && pk->req_ids != nullptr ? pk->num_listed : g.batch;
@@ -373,6 +381,16 @@ int launch_decode(const void* q, const int64_t* qs, const void* k_pool, const vo
   d.ws_counter = L.total ? reinterpret_cast<int32_t*>(ws) : nullptr;
   d.ws_ml = L.total ? reinterpret_cast<float*>(ws + L.counter_bytes) : nullptr;
   d.ws_o = L.total ? reinterpret_cast<float*>(ws + L.counter_bytes + L.ml_bytes) : nullptr;
+  d.k_new = fs != nullptr ? static_cast<const uint8_t*>(fs->k_new) : nullptr;
+  d.v_new = fs != nullptr ? static_cast<const uint8_t*>(fs->v_new) : nullptr;
+  d.k_sb = fs != nullptr ? fs->strides[0] : 0;
+  d.k_sh = fs != nullptr ? fs->strides[1] : 0;
+  d.k_st = fs != nullptr ? fs->strides[2] : 0;
+  d.v_sb = fs != nullptr ? fs->strides[3] : 0;
+  d.v_sh = fs != nullptr ? fs->strides[4] : 0;
+  d.v_st = fs != nullptr ? fs->strides[5] : 0;
+  d.k_pool = static_cast<uint8_t*>(const_cast<void*>(k_pool));
+  d.v_pool = static_cast<uint8_t*>(const_cast<void*>(v_pool));
   cudaError_t err = hyt::run_decode_attention(p, d, k_map, v_map, g.dtype, stream);
   if (err != cudaSuccess) return cuda_fail(err, "decode attention launch");
   return HYT_OK;
@@ -715,6 +733,46 @@ int hyt_paged_attention(const void* q, const int64_t* q_strides, const void* k_p
                           out_strides, scale, error_word, s);
   return launch_generic(q, q_strides, k_pool, v_pool, g, page_table, cache_lens, out,
                         out_strides, scale, error_word, s);
+}
+
+int hyt_paged_attention_scatter(const void* q, const int64_t* q_strides, const void* k_new,
+                                const void* v_new, const int64_t* new_strides, void* k_pool,
+                                void* v_pool, int32_t num_layers, int32_t layer,
+                                int64_t capacity_tokens, const int32_t* page_table,
+                                int32_t page_table_stride, const int32_t* cache_lens, void* out,
+                                const int64_t* out_strides, int32_t batch, int32_t query_len,
+                                int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                int32_t page_size, int32_t dtype, float scale, int32_t max_kv_len,
+                                int32_t split_tokens, void* workspace, size_t workspace_bytes,
+                                int32_t* error_word, void* stream) {
+  g_last_error.clear();
+  int rc = check_attention_pointers(q, q_strides, k_pool, v_pool, page_table, cache_lens, out,
+                                    out_strides);
+  if (rc != HYT_OK) return rc;
+  if (!k_new || !v_new || !new_strides) return fail(HYT_ERR_INVALID, "null pointer argument");
+  Geometry g{num_layers, layer, capacity_tokens, page_table_stride, batch, query_len,
+             num_q_heads, num_kv_heads, head_dim, page_size, dtype};
+  rc = check_geometry(g);
+  if (rc != HYT_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // one launch when the decode kernel serves the step and every new row is 16-byte aligned
+  bool rows16 = reinterpret_cast<uintptr_t>(k_new) % 16 == 0 && reinterpret_cast<uintptr_t>(v_new) % 16 == 0;
+  for (int i = 0; i < 6; ++i) rows16 = rows16 && (new_strides[i] * elem_bytes(dtype)) % 16 == 0;
+  if (decode_eligible(g) && rows16) {
+    const FusedScatter fs{k_new, v_new, new_strides};
+    return launch_decode(q, q_strides, k_pool, v_pool, g, page_table, cache_lens, out,
+                         out_strides, scale, max_kv_len, split_tokens, workspace,
+                         workspace_bytes, error_word, s, nullptr, &fs);
+  }
+  rc = hyt_kv_scatter(k_new, v_new, new_strides, k_pool, v_pool, num_layers, layer,
+                      capacity_tokens, page_table, page_table_stride, cache_lens, batch, query_len,
+                      num_kv_heads, head_dim, page_size, dtype, error_word, stream);
+  if (rc != HYT_OK) return rc;
+  return hyt_paged_attention(q, q_strides, k_pool, v_pool, num_layers, layer, capacity_tokens,
+                             page_table, page_table_stride, cache_lens, out, out_strides, batch,
+                             query_len, num_q_heads, num_kv_heads, head_dim, page_size, dtype,
+                             scale, max_kv_len, split_tokens, workspace, workspace_bytes,
+                             error_word, stream);
 }
 
 int hyt_kv_scatter_packed(const void* k_new, const void* v_new, const int64_t* new_strides,

@@ -21,6 +21,11 @@
 //     split writes its partial to the workspace and the last split to arrive
 //     (atomic counter, no waiting) merges all partials and resets the counter.
 //
+// Fused scatter (DecodeLaunch::k_new, uniform batches): the consumer warps of the split
+// that attends a new row first copy it from the step's K/V into its pool slot (the copy
+// kernel (a) makes) and fence the async proxy; the producer loads that tile only after
+// they have all arrived on an mbarrier. One launch then does write_layer + attend_layer.
+//
 // Packed batches: a launch may serve a list of requests (AttentionParams::req_ids)
 // whose one-token chunks sit on a shared token axis; workspace slots follow the
 // launch index, so the workspace is sized for the list.
@@ -87,7 +92,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRingBytes);
   uint64_t* empty = full + kStages;
-  int* s_last = reinterpret_cast<int*>(empty + kStages);
+  uint64_t* scattered = empty + kStages;  // fused scatter: the split's new rows are in the pool
+  int* s_last = reinterpret_cast<int*>(scattered + 1);
   volatile int* s_abort = s_last + 1;  // set once a bounded wait gave up
 
   // ---- refuse page ids / lengths that would address outside the pool
@@ -108,6 +114,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   bad = __syncthreads_or(bad);
   if (bad && threadIdx.x == 0) flag_error(p.error_word, bad);
   if (nsplits > P.d.max_splits) nsplits = P.d.max_splits;
+  // fused scatter: this split attends positions [new_lo, tok_end) of the step's new rows
+  // (a refused split writes nothing)
+  const int new_lo = max(cache_len, tok_begin);
+  const bool has_new = P.d.k_new != nullptr && !bad && new_lo < tok_end;
 
   if (threadIdx.x == 0) {
     *s_abort = 0;
@@ -115,6 +125,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
     }
+    mbar_init(scattered, kConsumerWarps * 32);
     fence_barrier_init();
   }
   __syncthreads();
@@ -136,6 +147,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int stage = i % kStages;
         if (i >= kStages) mbar_wait(&empty[stage], ((i / kStages) - 1) & 1, p.error_word, s_abort);
         const int tok = tok_begin + i * kTile;
+        // the tile holding the first new row is read only once the consumers wrote it
+        if (has_new && i == (new_lo - tok_begin) / kTile) mbar_wait(scattered, 0, p.error_word, s_abort);
         const int32_t page = table[tok >> p.page_shift];
         const int row = (page << p.page_shift) + (tok & page_mask);
         uint8_t* dst = smem + stage * kStageBytes;
@@ -151,6 +164,38 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   } else {
     // ------------------------------------------------------------ consumers
+    // fused scatter (kv_scatter's copy for this split's rows of KV head g), in two halves
+    // around the Q load so that its source loads and Q's share one memory round trip:
+    // up to kScatterPerThread 16-byte chunks per thread are loaded here and stored after
+    // the Q loads were issued, then a proxy fence lets the producer's TMA, ordered after
+    // the `scattered` barrier, read the new rows.
+    constexpr int kChunks = kD * int(sizeof(T)) / 16;
+    constexpr int kScatterPerThread = 2 * (kDecodeMaxRows * kChunks) / (kConsumerWarps * 32);
+    const int n_chunks = has_new ? 2 * (tok_end - new_lo) * kChunks : 0;
+    uint4 scat_v[kScatterPerThread];
+    uint8_t* scat_dst[kScatterPerThread];
+#pragma unroll
+    for (int c = 0; c < kScatterPerThread; ++c) {
+      const int idx = int(threadIdx.x) + c * kConsumerWarps * 32;
+      scat_dst[c] = nullptr;
+      if (idx < n_chunks) {
+        const int nrows = tok_end - new_lo;
+        const bool is_v = idx >= nrows * kChunks;
+        const int rem = is_v ? idx - nrows * kChunks : idx;
+        const int row = rem / kChunks, chunk = rem - row * kChunks;
+        const int pos = new_lo + row, t = pos - cache_len;
+        const int64_t src_elem = int64_t(b) * (is_v ? P.d.v_sb : P.d.k_sb) +
+                                 int64_t(g) * (is_v ? P.d.v_sh : P.d.k_sh) +
+                                 int64_t(t) * (is_v ? P.d.v_st : P.d.k_st);
+        scat_v[c] = *reinterpret_cast<const uint4*>((is_v ? P.d.v_new : P.d.k_new) +
+                                                    src_elem * int64_t(sizeof(T)) + chunk * 16);
+        const int32_t page = table[pos >> p.page_shift];  // checked with the split's pages
+        const int64_t slot = (int64_t(page) << p.page_shift) + (pos & page_mask);
+        const int64_t layer_off = int64_t(p.layer) * p.num_kv_heads * p.capacity * kD;
+        scat_dst[c] = (is_v ? P.d.v_pool : P.d.k_pool) +
+                      (layer_off + (int64_t(g) * p.capacity + slot) * kD) * int64_t(sizeof(T)) + chunk * 16;
+      }
+    }
     const int r0 = lane >> 2, c2 = (lane & 3) * 2;
     // Q rows: row r = local_head * query_len + t, zero past group * query_len.
     uint32_t qa[8][4];
@@ -179,6 +224,13 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
         }
       }
+    }
+    if (has_new) {  // second half of the fused scatter (see above)
+#pragma unroll
+      for (int c = 0; c < kScatterPerThread; ++c)
+        if (scat_dst[c] != nullptr) *reinterpret_cast<uint4*>(scat_dst[c]) = scat_v[c];
+      fence_proxy_async_global();
+      mbar_arrive(scattered);
     }
     // last visible key of each of this thread's two rows
     int limit[2];

@@ -101,6 +101,14 @@ struct DecodeLaunch {
   float* ws_o;           // [batch, H_kv, max_splits, rows, 128] f32 partial outputs
   float* ws_ml;          // [batch, H_kv, max_splits, rows, 2] f32 running max / sum
   int32_t* ws_counter;   // [batch, H_kv] arrival counters (zero between calls)
+  // Fused scatter (k_new != nullptr, uniform batches only): before attending, the step's
+  // new K/V rows [B, H_kv, T, 128] (element strides, rows 16-byte aligned) are written to
+  // their pool slots at positions cache_lens[b] + t, each by the split that attends it.
+  const uint8_t* k_new;
+  const uint8_t* v_new;
+  int64_t k_sb, k_sh, k_st, v_sb, v_sh, v_st;
+  uint8_t* k_pool;
+  uint8_t* v_pool;
 };
 constexpr int kDecodeMaxRows = 16;  // query rows per (request, kv head): group * query_len
 cudaError_t run_decode_attention(const AttentionParams& p, const DecodeLaunch& d,

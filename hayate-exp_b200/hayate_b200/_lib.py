@@ -36,6 +36,11 @@ SIGNATURES = {
                                       _c_i32, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
                                       _c_p, _c_p]),
     "hyt_paged_attention": (ctypes.c_int, _ATTENTION_ARGS + [_c_i32, _c_i32, _c_p, _c_size, _c_p, _c_p]),
+    "hyt_paged_attention_scatter": (ctypes.c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i32,
+                                                   _c_i32, _c_i64, _c_p, _c_i32, _c_p, _c_p, _c_p,
+                                                   _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
+                                                   _c_i32, _c_f32, _c_i32, _c_i32, _c_p, _c_size,
+                                                   _c_p, _c_p]),
     "hyt_decode_attention": (ctypes.c_int, _ATTENTION_ARGS + [_c_i32, _c_i32, _c_p, _c_size, _c_p, _c_p]),
     "hyt_decode_attention_noalloc": (ctypes.c_int, _ATTENTION_ARGS + [_c_i32, _c_i32, _c_p, _c_p]),
     "hyt_prefill_attention": (ctypes.c_int, _ATTENTION_ARGS + [_c_i32, _c_p, _c_p]),

@@ -196,6 +196,49 @@ def paged_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
     return out
 
 
+def paged_attention_scatter(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+                            k_pool: torch.Tensor, v_pool: torch.Tensor, layer: int,
+                            page_table: torch.Tensor, cache_lens: torch.Tensor, page_size: int,
+                            max_kv_len: int, scale: float | None = None,
+                            out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                            error_word: torch.Tensor | None = None,
+                            split_tokens: int = 0) -> torch.Tensor:
+    """``kv_scatter`` of the step's ``[B, H_kv, T, D]`` K/V, then ``paged_attention`` of
+    ``q``: one launch when the decode kernel serves the step (``hyt_paged_attention_scatter``)."""
+    _require_cuda(q, k_new, v_new, k_pool, v_pool, page_table, cache_lens)
+    num_layers, num_kv_heads, capacity, head_dim = _pool_geometry(k_pool, v_pool)
+    batch, num_q_heads, query_len, d = q.shape
+    if d != head_dim or q.dtype != k_pool.dtype:
+        raise ValueError("q must match the pool's head_dim and dtype")
+    if k_new.shape != v_new.shape or k_new.dtype != k_pool.dtype or v_new.dtype != k_pool.dtype:
+        raise ValueError("k/v must share one shape and the pool dtype")
+    if tuple(k_new.shape) != (batch, num_kv_heads, query_len, head_dim):
+        raise ValueError("k/v must be [batch, kv_heads, query_len, head_dim] of the pool")
+    if out is None:
+        out = torch.empty((batch, query_len, num_q_heads, head_dim), dtype=q.dtype,
+                          device=q.device).transpose(1, 2)
+    if out.shape != q.shape or out.dtype != q.dtype:
+        raise ValueError("out must match q")
+    qs = _lib.int64_array(_bht_strides(q, "q"))
+    os_ = _lib.int64_array(_bht_strides(out, "out"))
+    new_strides = _lib.int64_array(_bht_strides(k_new, "k") + _bht_strides(v_new, "v"))
+    pts = _table_args(page_table, cache_lens, batch)
+    scale = 1.0 / math.sqrt(head_dim) if scale is None else float(scale)
+    need = attention_workspace_bytes(batch, query_len, num_q_heads, num_kv_heads, head_dim,
+                                     max_kv_len, q.dtype, split_tokens)
+    if need and (workspace is None or workspace.numel() < need):
+        raise RuntimeError(f"attention needs a zeroed workspace of {need} bytes")
+    rc = _lib.lib().hyt_paged_attention_scatter(
+        q.data_ptr(), qs, k_new.data_ptr(), v_new.data_ptr(), new_strides, k_pool.data_ptr(),
+        v_pool.data_ptr(), num_layers, layer, capacity, page_table.data_ptr(), pts,
+        cache_lens.data_ptr(), out.data_ptr(), os_, batch, query_len, num_q_heads, num_kv_heads,
+        head_dim, page_size, dtype_code(q.dtype), scale, max_kv_len, split_tokens,
+        _ptr(workspace) if need else None, workspace.numel() if need else 0, _ptr(error_word),
+        _stream_ptr())
+    _lib.check(rc, "hyt_paged_attention_scatter")
+    return out
+
+
 # ---------------------------------------------------------------------------- packed batches
 def _th_strides(t: torch.Tensor, name: str) -> tuple[int, int]:
     """Element strides {token, head} of a ``[1, H, N, D]`` packed tensor."""

@@ -264,6 +264,31 @@ class PagedKVBatch:
                                    workspace=workspace, error_word=manager.error_word,
                                    kernel=manager.kernel, split_tokens=manager.split_tokens)
 
+    def write_attend_layer(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor,
+                           q: torch.Tensor) -> torch.Tensor:
+        """``write_layer(layer_idx, k, v)`` then ``attend_layer(q, layer_idx)``, the pair
+        hayate's attention layer calls back to back (``hayate/model/attention.py``), with the
+        same pool bytes and rows. A decode step runs as one launch: the decode kernel writes
+        the new K/V rows itself before reading them."""
+        manager = self._manager
+        if self.layout is not None or manager.kernel != "auto":
+            self.write_layer(layer_idx, k, v)
+            return self.attend_layer(q, layer_idx)
+        if k.shape[2] != self.query_len or v.shape != k.shape:
+            raise ValueError("k and v must be [batch, kv_heads, query_len, head_dim]")
+        if k.stride(-1) != 1:
+            k = k.contiguous()
+        if v.stride(-1) != 1:
+            v = v.contiguous()
+        if q.stride(-1) != 1:
+            q = q.contiguous()
+        workspace = manager.workspace_for(q.shape[0], self.query_len, q.shape[1], self.max_kv_len)
+        return ops.paged_attention_scatter(q, k, v, self.k_cache, self.v_cache, layer_idx,
+                                           self.page_table, self.cache_lens_i32, self.page_size,
+                                           self.max_kv_len, workspace=workspace,
+                                           error_word=manager.error_word,
+                                           split_tokens=manager.split_tokens)
+
     def _write_packed(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor) -> None:
         lay = self.layout
         if k.shape[0] != 1 or k.shape[2] != lay.total_tokens or v.shape != k.shape:

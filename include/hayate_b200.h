@@ -99,6 +99,27 @@ int hyt_paged_attention(const void* q, const int64_t* q_strides, const void* k_p
                         int32_t split_tokens, void* workspace, size_t workspace_bytes,
                         int32_t* error_word, void* stream);
 
+/*
+ * Write the step's new K/V rows, then attend: hyt_kv_scatter (k_new, v_new, new_strides
+ * as there) followed by hyt_paged_attention on the same stream, with the same results.
+ * Replaces PagedKVBatch.write_layer + attend_layer (hayate/engine/paged_cache.py:44-71),
+ * the pair hayate's attention layer calls back to back for every decode step. When the
+ * decode kernel serves the step and every new row is 16-byte aligned this is ONE launch:
+ * the split that attends a new row copies it into its pool slot first. Otherwise the two
+ * kernels run in turn. A split with a refused page id writes none of its new rows (the
+ * separate scatter would still write the rows whose pages are valid); both flag it.
+ */
+int hyt_paged_attention_scatter(const void* q, const int64_t* q_strides, const void* k_new,
+                                const void* v_new, const int64_t* new_strides, void* k_pool,
+                                void* v_pool, int32_t num_layers, int32_t layer,
+                                int64_t capacity_tokens, const int32_t* page_table,
+                                int32_t page_table_stride, const int32_t* cache_lens, void* out,
+                                const int64_t* out_strides, int32_t batch, int32_t query_len,
+                                int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                int32_t page_size, int32_t dtype, float scale, int32_t max_kv_len,
+                                int32_t split_tokens, void* workspace, size_t workspace_bytes,
+                                int32_t* error_word, void* stream);
+
 /* Split-KV decode kernel only (query_len * (H_q / H_kv) <= 16, bf16/f16, D = 128).
  * split_tokens: tokens per split, a multiple of 64; 0 picks one for this GPU. */
 int hyt_decode_attention(const void* q, const int64_t* q_strides, const void* k_pool,
