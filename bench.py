@@ -212,6 +212,20 @@ def sum_over_ranks(value: float, world: int) -> float:
     return value if world == 1 else _reduce(value, "SUM")
 
 
+def gather_over_ranks(value: float, world: int) -> list:
+    """Every rank's value, in rank order (e.g. each rank's output checksum)."""
+    if world == 1:
+        return [value]
+    import torch
+    import torch.distributed as dist
+
+    device = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    mine = torch.tensor([value], dtype=torch.float64, device=device)
+    parts = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(parts, mine)
+    return [float(t.item()) for t in parts]
+
+
 # ---------------------------------------------------------------------------- decode (cfg 2)
 def build_decode(rank: int, split_tokens: int, requests: int = 64):
     import torch
@@ -292,6 +306,7 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
     ms_local = start.elapsed_time(end)
     kernel_ms = sum(a.elapsed_time(b) for a, b in kern) / args.steps
     manager.check_device_errors()
+    checksums = gather_over_ranks(float(out.double().sum().item()), world)
     ms_total = max_over_ranks(ms_local, world)
     total_bytes = sum_over_ranks(float(step_bytes), world)
     value = total_bytes * args.steps / (ms_total / 1e3) / 1e9
@@ -351,6 +366,7 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
                      "kernel": "decode_attention_kernel (split-KV decode with the fused row scatter)"},
         "gpu_launches": args.steps,
         "clocks": clocks.summary(),
+        "output_checksums": [round(c, 6) for c in checksums],
     }
     if args.reference_gpu and rank == 0:
         ref_gpu = reference_gpu_compare(manager, handles, q, k, v, out, kv_bytes / 1e9, "GB_s")
@@ -608,12 +624,14 @@ def run_longdecode(args, world, rank, local, peaks, peak_kind):
               for s in range(steps + args.warmup)]
     torch.cuda.synchronize()
 
+    last = [None]
+
     def step(s, ev=None):
         batch = manager.begin_batch(handles, 1)
         q, k, v = inputs[s]
         if ev is not None:
             ev[0].record()
-        batch.write_attend_layer(0, k, v, q)  # one launch: the decode kernel writes the rows
+        last[0] = batch.write_attend_layer(0, k, v, q)  # one launch: the decode kernel writes the rows
         if ev is not None:
             ev[1].record()
         manager.commit_batch(handles, 1)
@@ -637,6 +655,7 @@ def run_longdecode(args, world, rank, local, peaks, peak_kind):
     manager.check_device_errors()
     ms = max_over_ranks(start.elapsed_time(end), world)
     attn_ms = sum(a.elapsed_time(b) for a, b in evs) / steps
+    checksums = gather_over_ranks(float(last[0].double().sum().item()), world)
     row = 8 * 128 * 2 * 2  # K + V bytes per token
     unique_per_step = sum(len(groups) * (LONG_PREFIX + LONG_PER_GROUP * (own + s + 1)) for s in range(steps)) * row / steps
     logical_per_step = sum(n_req * (LONG_CONTEXT + s + 1) for s in range(steps)) * row / steps
@@ -661,6 +680,7 @@ def run_longdecode(args, world, rank, local, peaks, peak_kind):
         "attention_ms_per_step": round(attn_ms, 4),
         "gpu_launches": steps,
         "clocks": clocks.summary(),
+        "output_checksums": [round(c, 6) for c in checksums],
     }
 
 

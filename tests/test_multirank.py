@@ -39,6 +39,8 @@ def _worker(rank: int, world: int, port: int, out):
         # job time = the slowest rank, job work = the sum over ranks
         result["max"] = bench.max_over_ranks(1.5 + rank, world)
         result["sum"] = bench.sum_over_ranks(10.0 * (rank + 1), world)
+        # per-rank output checksums gathered in rank order
+        result["gather"] = bench.gather_over_ranks(100.0 + rank, world)
         # config 5: whole prefix groups per rank
         groups = bench.long_groups(rank, world)
         result["groups"] = groups
@@ -78,6 +80,7 @@ def test_two_gloo_ranks(world):
     for r in range(world):
         assert res[r]["max"] == 1.5 + world - 1
         assert res[r]["sum"] == sum(10.0 * (k + 1) for k in range(world))
+        assert res[r]["gather"] == [100.0 + k for k in range(world)]
         assert res[r]["free"]
         assert all(x == 4 for x in res[r]["refs"][0::2])   # prefix page held by 1 + 3 requests
         assert all(x == 3 for x in res[r]["refs"][1::2])   # 2 prefix pages + 1 private page
