@@ -573,6 +573,7 @@ def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=N
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
                      "frac_of_sustained": round(achieved / peaks["bf16_tflops_sustained"], 4),
+                     "nominal_frac_2250": round(achieved / 2250.0, 4),
                      "peak_source": f"{peak_kind} bf16_tflops (burst)",
                      "traffic": PREFILL_CFG3_TRAFFIC if prefix_max == 4096 else None,
                      "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + write.sum)",
