@@ -4,7 +4,10 @@
 // sizing and the choice between the decode, prefill and CUDA-core kernels.
 // Every entry point only enqueues work on the caller's stream.
 #include <algorithm>
+#include <functional>
 #include <mutex>
+#include <queue>
+#include <vector>
 #include <string>
 
 #include "common.cuh"
@@ -414,7 +417,8 @@ bool prefill_eligible(const Geometry& g, const void* q, const int64_t* qs, const
 int launch_prefill(const void* q, const int64_t* qs, const void* k_pool, const void* v_pool,
                    const Geometry& g, const int32_t* page_table, const int32_t* cache_lens,
                    void* out, const int64_t* os, float scale, int32_t* error_word,
-                   cudaStream_t stream, const PackedArgs* pk = nullptr) {
+                   cudaStream_t stream, const PackedArgs* pk = nullptr,
+                   const hyt::PrefillPlan* plan = nullptr) {
   const int32_t count = pk != nullptr && pk->req_ids != nullptr ? pk->num_listed : g.batch;
   if (count > 65535 || g.num_q_heads > 65535) return fail(HYT_ERR_UNSUPPORTED, "batch too large");
   CUtensorMap k_map, v_map;
@@ -432,7 +436,7 @@ int launch_prefill(const void* q, const int64_t* qs, const void* k_pool, const v
   const bool q_tma = q_tensor_map(q, qs, g.dtype, packed ? pk->total_tokens : g.query_len,
                                   g.num_q_heads, packed ? 1 : g.batch, &q_map, &q_ht);
   cudaError_t err = hyt::run_prefill_attention(p, k_map, v_map, q_tma ? &q_map : nullptr, q_ht,
-                                               g.dtype, stream);
+                                               g.dtype, stream, plan);
   if (err != cudaSuccess) return cuda_fail(err, "prefill attention launch");
   return HYT_OK;
 }
@@ -449,6 +453,52 @@ int launch_generic(const void* q, const int64_t* qs, const void* k_pool, const v
   cudaError_t err = hyt::run_generic_attention(p, g.dtype, stream);
   if (err != cudaSuccess) return cuda_fail(err, "generic attention launch");
   return HYT_OK;
+}
+
+// ------------------------------------------------------------------ prefill schedule
+// Cost model of one prefill work item, in key tiles: the tiles it streams plus a fixed
+// start-up/epilogue cost; a half of a split item pays the start-up again and its share of
+// the merge. Measured per CTA on config 3: ~2 us per key tile, ~5 us of start-up and
+// epilogue.
+constexpr double kItemOverhead = 2.5, kMergeCost = 0.5;
+
+struct PlanEntry {
+  int32_t z, q_tile, pair, k_lo, k_hi, split;  // split: slot * 2 + part, or -1
+  double cost;
+};
+
+// Longest time any of `sms` SMs is busy when the items start in `order` on whichever SM
+// frees first (the block scheduler's greedy order, one CTA per SM).
+double greedy_makespan(const std::vector<double>& costs, int sms) {
+  std::priority_queue<double, std::vector<double>, std::greater<double>> free_at;
+  for (int i = 0; i < sms; ++i) free_at.push(0.0);
+  double end = 0.0;
+  for (double c : costs) {
+    const double t = free_at.top() + c;
+    free_at.pop();
+    free_at.push(t);
+    end = std::max(end, t);
+  }
+  return end;
+}
+
+// Items of the default grid, in its launch order (request, head pair, query tile from the
+// last), with their key-tile counts; false when a count does not fit the item encoding.
+bool prefill_items(const int32_t* cache_lens, const int32_t* q_lens, int32_t batch,
+                   int32_t query_len, int32_t pairs, std::vector<PlanEntry>* items) {
+  for (int32_t z = 0; z < batch; ++z) {
+    const int64_t ql = q_lens != nullptr ? q_lens[z] : query_len;
+    if (ql <= 0 || cache_lens[z] < 0) continue;
+    const int32_t tiles = int32_t((ql + 127) / 128);
+    for (int32_t pair = 0; pair < pairs; ++pair)
+      for (int32_t qt = tiles - 1; qt >= 0; --qt) {
+        const int64_t t_last = std::min<int64_t>(int64_t(qt) * 128 + 127, ql - 1);
+        const int64_t n = (int64_t(cache_lens[z]) + t_last) / 128 + 1;
+        if (n > 0xFFFF || qt > 0xFFFF || pair > 0xFFFF) return false;
+        items->push_back({z, qt, pair, 0, int32_t(n), -1, double(n) + kItemOverhead});
+      }
+  }
+  return true;
 }
 
 // ------------------------------------------------------------------ static decode scratch
@@ -950,6 +1000,125 @@ int hyt_paged_attention_packed(const void* q, const int64_t* q_strides, const vo
                           error_word, st, &pk);
   }
   return rc;
+}
+
+int32_t hyt_prefill_plan(const int32_t* cache_lens, const int32_t* q_lens, int32_t batch,
+                         int32_t query_len, int32_t num_q_heads, int32_t num_sms,
+                         int32_t max_splits, int32_t* items, int32_t max_items,
+                         int32_t* num_splits) {
+  g_last_error.clear();
+  if (cache_lens == nullptr || items == nullptr || num_splits == nullptr)
+    return fail(HYT_ERR_INVALID, "null pointer argument");
+  if (batch < 1 || num_q_heads < 2 || num_sms < 1 || max_splits < 0 || max_items < 0 ||
+      (q_lens == nullptr && query_len < 1))
+    return fail(HYT_ERR_INVALID, "bad plan sizes");
+  *num_splits = 0;
+  std::vector<PlanEntry> base;
+  if (!prefill_items(cache_lens, q_lens, batch, query_len, num_q_heads / 2, &base)) return 0;
+  if (base.empty()) return 0;
+  std::vector<double> costs;
+  for (const PlanEntry& e : base) costs.push_back(e.cost);
+  double best = greedy_makespan(costs, num_sms);  // the default grid
+  int best_k = -1;
+  // longest first, the k heaviest items cut in two along their keys
+  std::vector<PlanEntry> lpt = base;
+  std::stable_sort(lpt.begin(), lpt.end(),
+                   [](const PlanEntry& a, const PlanEntry& b) { return a.cost > b.cost; });
+  int splittable = 0;
+  for (const PlanEntry& e : lpt) splittable += e.k_hi >= 2;
+  auto build = [&](int k, std::vector<PlanEntry>* out) {
+    out->clear();
+    int slot = 0;
+    for (const PlanEntry& e : lpt) {
+      if (slot < k && e.k_hi >= 2) {
+        const int32_t mid = e.k_hi / 2;
+        const double c0 = mid + kItemOverhead + kMergeCost, c1 = (e.k_hi - mid) + kItemOverhead + kMergeCost;
+        out->push_back({e.z, e.q_tile, e.pair, 0, mid, slot * 2, c0});
+        out->push_back({e.z, e.q_tile, e.pair, mid, e.k_hi, slot * 2 + 1, c1});
+        ++slot;
+      } else {
+        out->push_back(e);
+      }
+    }
+    std::stable_sort(out->begin(), out->end(),
+                     [](const PlanEntry& a, const PlanEntry& b) { return a.cost > b.cost; });
+  };
+  std::vector<PlanEntry> cand;
+  const int limit = std::min(max_splits, splittable);
+  for (int k : {0, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256, 384, 512}) {
+    if (k > limit) break;
+    if (int64_t(base.size()) + k > max_items) break;
+    build(k, &cand);
+    costs.clear();
+    for (const PlanEntry& e : cand) costs.push_back(e.cost);
+    const double m = greedy_makespan(costs, num_sms);
+    if (m < best - 1e-9) {
+      best = m;
+      best_k = k;
+    }
+  }
+  if (best_k < 0) return 0;  // the default grid is as good: no plan
+  build(best_k, &cand);
+  for (size_t i = 0; i < cand.size(); ++i) {
+    const PlanEntry& e = cand[i];
+    items[4 * i + 0] = e.z;
+    items[4 * i + 1] = e.q_tile | (e.pair << 16);
+    items[4 * i + 2] = e.k_lo | (e.k_hi << 16);
+    items[4 * i + 3] = e.split;
+  }
+  *num_splits = best_k;
+  return int32_t(cand.size());
+}
+
+// Split workspace: [counters (int32 per slot, 256-byte padded) | (max, sum) | partial O].
+static size_t prefill_counter_bytes(int32_t num_splits) { return (size_t(num_splits) * 4 + 255) / 256 * 256; }
+
+size_t hyt_prefill_workspace_bytes(int32_t num_splits) {
+  if (num_splits <= 0) return 0;
+  return prefill_counter_bytes(num_splits) + size_t(num_splits) * size_t(hyt::kPrefillSplitSlotBytes);
+}
+
+int hyt_prefill_attention_planned(const void* q, const int64_t* q_strides, const void* k_pool,
+                                  const void* v_pool, int32_t num_layers, int32_t layer,
+                                  int64_t capacity_tokens, const int32_t* page_table,
+                                  int32_t page_table_stride, const int32_t* cache_lens, void* out,
+                                  const int64_t* out_strides, int32_t batch, int32_t query_len,
+                                  int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                  int32_t page_size, int32_t dtype, float scale,
+                                  const int32_t* items, int32_t num_items, int32_t num_splits,
+                                  void* workspace, size_t workspace_bytes, int32_t* error_word,
+                                  void* stream) {
+  g_last_error.clear();
+  int rc = check_attention_pointers(q, q_strides, k_pool, v_pool, page_table, cache_lens, out,
+                                    out_strides);
+  if (rc != HYT_OK) return rc;
+  Geometry g{num_layers, layer, capacity_tokens, page_table_stride, batch, query_len,
+             num_q_heads, num_kv_heads, head_dim, page_size, dtype};
+  rc = check_geometry(g);
+  if (rc != HYT_OK) return rc;
+  if (!prefill_eligible(g, q, q_strides, out, out_strides))
+    return fail(HYT_ERR_UNSUPPORTED,
+                "prefill kernel needs bf16/f16, head_dim 128, page_size % 128 == 0, an even "
+                "query-head group and 16-byte aligned q/out rows");
+  if (num_items < 0 || num_splits < 0 || (num_items > 0 && items == nullptr))
+    return fail(HYT_ERR_INVALID, "bad plan");
+  if (num_splits > 0 && (workspace == nullptr || workspace_bytes < hyt_prefill_workspace_bytes(num_splits)))
+    return fail(HYT_ERR_WORKSPACE, "workspace missing or smaller than hyt_prefill_workspace_bytes()");
+  if (num_items == 0)  // no plan: the default grid
+    return launch_prefill(q, q_strides, k_pool, v_pool, g, page_table, cache_lens, out,
+                          out_strides, scale, error_word, static_cast<cudaStream_t>(stream));
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  hyt::PrefillPlan plan;
+  plan.items = reinterpret_cast<const hyt::PrefillItem*>(items);
+  plan.num_items = num_items;
+  plan.num_splits = num_splits;
+  const size_t cb = prefill_counter_bytes(num_splits), ml_bytes = size_t(num_splits) * 2 * 2 * 128 * 2 * 4;
+  plan.ws_counter = num_splits > 0 ? reinterpret_cast<int32_t*>(ws) : nullptr;
+  plan.ws_ml = num_splits > 0 ? reinterpret_cast<float*>(ws + cb) : nullptr;
+  plan.ws_o = num_splits > 0 ? reinterpret_cast<float*>(ws + cb + ml_bytes) : nullptr;
+  return launch_prefill(q, q_strides, k_pool, v_pool, g, page_table, cache_lens, out,
+                        out_strides, scale, error_word, static_cast<cudaStream_t>(stream), nullptr,
+                        &plan);
 }
 
 size_t hyt_attention_workspace_bytes(int32_t batch, int32_t query_len, int32_t num_q_heads,

@@ -117,12 +117,32 @@ cudaError_t run_decode_attention(const AttentionParams& p, const DecodeLaunch& d
 
 // ------------------------------------------------------------ (b) tcgen05 chunked prefill
 // bf16/f16, head_dim 128, page_size % 128 == 0, q/out rows 16-byte aligned.
+// Planned schedule (optional): the grid is plan.num_items CTAs, CTA i computing item
+// plan.items[i] = {z (launch request index), query tile | head pair << 16, first key
+// tile | end key tile << 16, split}. split = slot * 2 + part for one half of an item cut
+// in two along its keys, -1 for a whole item; the two halves write their partial
+// (O, max, sum) into slot `slot` of the split workspace and the second to arrive merges
+// them (atomic counter per slot, no waiting) and resets the counter.
+struct PrefillItem {
+  int32_t z, tile_pair, keys, split;
+};
+struct PrefillPlan {
+  const PrefillItem* items;  // device; nullptr: the default grid
+  int32_t num_items;
+  int32_t num_splits;   // slots the workspace holds
+  float* ws_o;          // [slots, 2 parts, 2 heads, 32 column chunks, 128 rows, 4] f32
+  float* ws_ml;         // [slots, 2 parts, 2 heads, 128 rows, 2] f32 (max, sum)
+  int32_t* ws_counter;  // [slots] arrival counters (zero between calls)
+};
+constexpr int64_t kPrefillSplitSlotBytes = 2 * (2 * 128 * 128 * 4 + 2 * 128 * 2 * 4);
+
 // q_map (optional): a 4-D tensor map over q, dims (head_dim, T, H_q, B) or, with q_ht,
 // (head_dim, H_q, T, B), box 64 x 128 rows, 128-byte swizzle; T is query_len (the token
 // axis for packed batches, B = 1). Without it the softmax warps load Q themselves.
 cudaError_t run_prefill_attention(const AttentionParams& p, const CUtensorMap& k_map,
                                   const CUtensorMap& v_map, const CUtensorMap* q_map, bool q_ht,
-                                  int dtype, cudaStream_t stream);
+                                  int dtype, cudaStream_t stream,
+                                  const PrefillPlan* plan = nullptr);
 
 // ------------------------------------------------------------ fused QK-norm + RoPE + scatter
 struct NormRopeParams {

@@ -61,6 +61,7 @@ constexpr int kKeys = 128;  // keys per KV tile
 constexpr int kD = 128;
 constexpr int kSoftmaxThreads = 512;  // 8 warps per tile
 constexpr int kProducerWarp = 16, kMmaWarp = 17;
+constexpr int kSoftmaxBar = 9;  // named barrier of all 16 softmax warps (1..8: row-quarter pairs)
 constexpr int kThreads = 576;
 constexpr int kTileBytes = kRows * kD * 2;   // 32 KB
 constexpr int kChunkBytes = kTileBytes / 2;  // [128 rows x 64 elements]
@@ -80,6 +81,7 @@ constexpr int kPrefetchTiles = 3;          // L2 prefetch distance of the K/V st
 
 struct PrefillKernelParams {
   AttentionParams a;
+  PrefillPlan plan;  // items == nullptr: the default grid (query tile, head pair, request)
   int32_t group;
   int32_t q_tma;  // Q arrives by TMA through q_map (else the softmax warps load it)
   int32_t q_ht;   // q_map's dims are (d, head, token, request), else (d, token, head, request)
@@ -132,8 +134,46 @@ struct Barriers {
   uint32_t tmem_base;
   int32_t abort;  // set once a bounded wait gave up: later waits return at once
   int32_t bad;    // device error bits of a refused page table: the CTA writes zeros
+  int32_t last;   // split item: this half arrived second and merges the two
 };
 static_assert(sizeof(Barriers) <= 256, "barrier block");
+
+// Split items: both halves' partials are in the workspace; write out = (O0 a0 + O1 a1) /
+// (l0 a0 + l1 a1), a_i = 2^(m_i - max(m0, m1)), for rows t0 .. of heads h0, h0 + 1. A half
+// with l = 0 (nothing visible, or refused) contributes nothing. Threads tid, tid + nthreads
+// ... take (head, 16-byte column chunk, row) entries, consecutive threads consecutive rows.
+template <typename T, typename RowFn>
+__device__ __forceinline__ void merge_split(const PrefillPlan& plan, int slot, const AttentionParams& p,
+                                            int h0, int t0, int query_len, RowFn o_row, int tid,
+                                            int nthreads) {
+  const float4* wo = reinterpret_cast<const float4*>(plan.ws_o);
+  const float2* ml = reinterpret_cast<const float2*>(plan.ws_ml);
+  for (int idx = tid; idx < 2 * 32 * kRows; idx += nthreads) {
+    const int r = idx & (kRows - 1), c4 = (idx >> 7) & 31, x = idx >> 12;
+    if (t0 + r >= query_len) continue;
+    const int64_t u0 = (int64_t(slot) * 2 + 0) * 2 + x, u1 = (int64_t(slot) * 2 + 1) * 2 + x;
+    const float2 a = __ldcg(&ml[u0 * kRows + r]), c = __ldcg(&ml[u1 * kRows + r]);
+    const bool use0 = a.y > 0.f, use1 = c.y > 0.f;
+    const float m = use0 && use1 ? fmaxf(a.x, c.x) : (use0 ? a.x : (use1 ? c.x : 0.f));
+    const float f0 = use0 ? ex2(a.x - m) : 0.f, f1 = use1 ? ex2(c.x - m) : 0.f;
+    const float l = a.y * f0 + c.y * f1;
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (use0) {
+      const float4 v = __ldcg(&wo[(u0 * 32 + c4) * kRows + r]);
+      o = make_float4(v.x * f0, v.y * f0, v.z * f0, v.w * f0);
+    }
+    if (use1) {
+      const float4 v = __ldcg(&wo[(u1 * 32 + c4) * kRows + r]);
+      o = make_float4(o.x + v.x * f1, o.y + v.y * f1, o.z + v.z * f1, o.w + v.w * f1);
+    }
+    uint2 w;
+    w.x = Elem<T>::pack2(o.x * inv, o.y * inv);
+    w.y = Elem<T>::pack2(o.z * inv, o.w * inv);
+    T* out = static_cast<T*>(p.out) + o_row(t0 + r) + int64_t(h0 + x) * p.o_sh + c4 * 4;
+    *reinterpret_cast<uint2*>(out) = w;
+  }
+}
 
 // 96 registers: 18 warps over 4 sub-partitions put 5 warps on one 16K-register file.
 template <typename T, bool kPacked>
@@ -144,9 +184,28 @@ __global__ void __maxnreg__(96)
                              const PrefillKernelParams P) {
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   const AttentionParams& p = P.a;
-  // heavier (later) query tiles first: they see the most keys
-  const int q_tile = int(gridDim.x) - 1 - int(blockIdx.x);
-  const int pair = blockIdx.y, b = kPacked ? att_request(p, blockIdx.z) : int(blockIdx.z);
+  // work item: from the default grid, or planned (item check uniform per CTA)
+  int q_tile, pair, z, k_first = 0, k_end = 1 << 30, split = -1;
+  bool item_ok = true;
+  if (P.plan.items != nullptr) {
+    const PrefillItem it = P.plan.items[blockIdx.x];
+    z = it.z;
+    q_tile = it.tile_pair & 0xFFFF;
+    pair = int(uint32_t(it.tile_pair) >> 16);
+    k_first = it.keys & 0xFFFF;
+    k_end = int(uint32_t(it.keys) >> 16);
+    split = it.split;
+    if (split >= 0 && (split >> 1) >= P.plan.num_splits) {  // no slot to report through
+      if (threadIdx.x == 0) flag_error(p.error_word, HYT_DEVERR_PLAN_RANGE);
+      return;
+    }
+    item_ok = z >= 0 && z < att_launch_count(p) && pair < p.num_q_heads / 2 && k_first < k_end;
+  } else {
+    q_tile = int(gridDim.x) - 1 - int(blockIdx.x);  // heavier (later) query tiles first
+    pair = blockIdx.y;
+    z = blockIdx.z;
+  }
+  const int b = !item_ok ? 0 : (kPacked ? att_request(p, z) : z);
   const int h0 = pair * 2;  // tiles A and B: heads h0 and h0 + 1 of KV group g
   const int g = h0 / P.group;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -155,13 +214,6 @@ __global__ void __maxnreg__(96)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Barriers* bars = reinterpret_cast<Barriers*>(smem + kBarOff);
 
-  // packed batches: this request's chunk length; tiles past it have no work (uniform
-  // per CTA, decided before any barrier or TMEM allocation)
-  if (kPacked && !att_request_ok(p, b)) {
-    if (q_tile == 0 && pair == 0 && threadIdx.x == 0) flag_error(p.error_word, HYT_DEVERR_PACKED_RANGE);
-    return;
-  }
-  const int query_len = kPacked ? p.q_len[b] : p.query_len;
   // element offsets of query row t of this request in q and in out (head offset apart)
   auto q_row = [&](int t) -> int64_t {
     return kPacked ? (int64_t(p.q_start[b]) + t) * p.q_st : int64_t(b) * p.q_sb + int64_t(t) * p.q_st;
@@ -170,7 +222,43 @@ __global__ void __maxnreg__(96)
     return kPacked ? (int64_t(p.q_start[b]) + t) * p.o_st : int64_t(b) * p.o_sb + int64_t(t) * p.o_st;
   };
   const int t0 = q_tile * kRows;
-  if (t0 >= query_len) return;
+  // A half of a split item with nothing to contribute still takes its turn in the slot's
+  // protocol: an empty partial (sum 0), then, if it arrived second, the merge.
+  auto empty_split = [&](bool rows_known, int query_len) {
+    if (split < 0) return;
+    const int slot = split >> 1, part = split & 1;
+    float2* ml = reinterpret_cast<float2*>(P.plan.ws_ml) + (int64_t(slot) * 2 + part) * 2 * kRows;
+    for (int i = threadIdx.x; i < 2 * kRows; i += kThreads) ml[i] = make_float2(-INFINITY, 0.f);
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) bars->last = atomicAdd(&P.plan.ws_counter[slot], 1) == 1;
+    __syncthreads();
+    if (bars->last) {
+      __threadfence();
+      if (rows_known) merge_split<T>(P.plan, slot, p, h0, t0, query_len, o_row, threadIdx.x, kThreads);
+      if (threadIdx.x == 0) P.plan.ws_counter[slot] = 0;
+    }
+  };
+  if (!item_ok) {
+    if (threadIdx.x == 0) flag_error(p.error_word, HYT_DEVERR_PLAN_RANGE);
+    empty_split(false, 0);
+    return;
+  }
+
+  // packed batches: this request's chunk length; tiles past it have no work (uniform
+  // per CTA, decided before any barrier or TMEM allocation)
+  if (kPacked && !att_request_ok(p, b)) {
+    if ((q_tile == 0 && pair == 0) || P.plan.items != nullptr)
+      if (threadIdx.x == 0) flag_error(p.error_word, HYT_DEVERR_PACKED_RANGE);
+    empty_split(false, 0);
+    return;
+  }
+  const int query_len = kPacked ? p.q_len[b] : p.query_len;
+  if (t0 >= query_len) {
+    if (P.plan.items != nullptr && threadIdx.x == 0) flag_error(p.error_word, HYT_DEVERR_PLAN_RANGE);
+    empty_split(false, 0);
+    return;
+  }
   const int cache_len = p.cache_lens[b];
   const int t_last = min(t0 + kRows, query_len) - 1;
   const int n_tiles = (cache_len + t_last) / kKeys + 1;
@@ -190,6 +278,16 @@ __global__ void __maxnreg__(96)
         out[d] = Elem<T>::from_float(0.f);
       }
     }
+    __syncthreads();  // the zeros before a merge that may overwrite them
+    empty_split(true, query_len);
+    return;
+  }
+  // key tiles [k_lo, k_lo + n_loop) of the item's n_tiles (all of them unless split)
+  const int k_lo = k_first;
+  const int n_loop = min(k_end, n_tiles) - k_first;
+  if (n_loop <= 0) {
+    if (threadIdx.x == 0) flag_error(p.error_word, HYT_DEVERR_PLAN_RANGE);
+    empty_split(true, query_len);
     return;
   }
 
@@ -271,11 +369,11 @@ __global__ void __maxnreg__(96)
       // No prefetch burst at start-up: the whole first wave loads Q and its first tiles
       // then, sharing HBM. Once a page id is refused, later stages are released without a
       // load (plain arrivals) so every role still walks the same number of tiles.
-      for (int j = 0; j < n_tiles; ++j) {
+      for (int j = 0; j < n_loop; ++j) {  // ring position j holds key tile k_lo + j
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
-        if (!bad && j >= 1 && j + kPrefetchTiles < n_tiles) prefetch(j + kPrefetchTiles);
-        const int row = bad ? -1 : tile_row(j, bad);
+        if (!bad && j >= 1 && j + kPrefetchTiles < n_loop) prefetch(k_lo + j + kPrefetchTiles);
+        const int row = bad ? -1 : tile_row(k_lo + j, bad);
         if (j >= 2) mbar_wait(&bars->k_empty[st], ph ^ 1, err, abort);
         uint8_t* kdst = smem + kKOff + st * kTileBytes;
         if (!bad) {
@@ -300,7 +398,7 @@ __global__ void __maxnreg__(96)
         bars->bad = bad;
       }
       mbar_arrive(&bars->prod_done);  // release: `bad` is visible to whoever waits on it
-      for (int j = max(0, n_tiles - 2); j < n_tiles; ++j) {  // nothing in flight at exit
+      for (int j = max(0, n_loop - 2); j < n_loop; ++j) {  // nothing in flight at exit
         mbar_drain(&bars->k_full[j & 1], (j >> 1) & 1);
         mbar_drain(&bars->v_full[j & 1], (j >> 1) & 1);
       }
@@ -366,8 +464,8 @@ __global__ void __maxnreg__(96)
     mbar_wait(&bars->k_full[0], 0, err, abort);
     issue(0, 0, false, true, nullptr, nullptr);
     issue(1, 0, false, true, &bars->k_empty[0], nullptr);
-    for (int j = 0; j < n_tiles; ++j) {
-      const bool more = j + 1 < n_tiles;
+    for (int j = 0; j < n_loop; ++j) {
+      const bool more = j + 1 < n_loop;
       mbar_wait(&bars->v_full[j & 1], (j >> 1) & 1, err, abort);
       mbar_wait(&bars->p_full[0], j & 1, err, abort);  // tile A
       if (more) mbar_wait(&bars->k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, err, abort);
@@ -429,7 +527,7 @@ __global__ void __maxnreg__(96)
     const uint32_t p_col = x * 128 + half * 32;
     const uint32_t o_col = kOCol + x * 128 + half * 64;
     float m_run = -INFINITY, l_run = 0.f;
-    for (int j = 0; j < n_tiles; ++j) {
+    for (int j = 0; j < n_loop; ++j) {
       mbar_wait(&bars->s_full[x], j & 1, err, abort);
       tc_fence_after();
       float s[64];
@@ -444,7 +542,7 @@ __global__ void __maxnreg__(96)
           for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(raw[c][i]);
       }
       // mask + this half's row max on the raw scores (scale > 0 keeps the order)
-      const int key0 = j * kKeys + half * 64;
+      const int key0 = (k_lo + j) * kKeys + half * 64;
       if (key0 + 63 > limit) {  // only the diagonal tiles
 #pragma unroll
         for (int c = 0; c < 64; ++c)
@@ -494,9 +592,39 @@ __global__ void __maxnreg__(96)
     tc_fence_after();
     named_bar_sync(pair_bar, 64);
     const float l = red_sum[r] + red_sum[kRows + r];
-    const float inv = l > 0.f ? 1.f / l : 0.f;
     // a refused page table: zeros (`bad` is published by the producer's prod_done arrival)
     const bool refused = *reinterpret_cast<volatile int32_t*>(&bars->bad) != 0;
+    if (split >= 0) {
+      // one half of a split item: its partial (O, running max, sum) goes to the workspace
+      // (consecutive lanes -> consecutive rows of a 16-byte column chunk); the half that
+      // arrives second merges both and resets the slot's counter. A refused half adds 0.
+      const int slot = split >> 1, part = split & 1;
+      const int64_t unit = (int64_t(slot) * 2 + part) * 2 + x;
+      float4* wo = reinterpret_cast<float4*>(P.plan.ws_o) + unit * 32 * kRows;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t o[32];
+        tmem_ld32(lane_addr + o_col + c * 32, o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int v = 0; v < 8; ++v)
+          wo[(half * 16 + c * 8 + v) * kRows + r] =
+              make_float4(__uint_as_float(o[4 * v]), __uint_as_float(o[4 * v + 1]),
+                          __uint_as_float(o[4 * v + 2]), __uint_as_float(o[4 * v + 3]));
+      }
+      if (half == 0)
+        reinterpret_cast<float2*>(P.plan.ws_ml)[unit * kRows + r] = make_float2(m_run, refused ? 0.f : l);
+      __threadfence();
+      named_bar_sync(kSoftmaxBar, kSoftmaxThreads);
+      if (threadIdx.x == 0) bars->last = atomicAdd(&P.plan.ws_counter[slot], 1) == 1;
+      named_bar_sync(kSoftmaxBar, kSoftmaxThreads);
+      if (*reinterpret_cast<volatile int32_t*>(&bars->last)) {
+        __threadfence();
+        merge_split<T>(P.plan, slot, p, h0, t0, query_len, o_row, threadIdx.x, kSoftmaxThreads);
+        if (threadIdx.x == 0) P.plan.ws_counter[slot] = 0;
+      }
+    } else {
+    const float inv = l > 0.f ? 1.f / l : 0.f;
     uint8_t* stage = smem + kKOff + x * kRows * kStageRowBytes + half * 128;
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
@@ -522,6 +650,7 @@ __global__ void __maxnreg__(96)
       const uint4 w = *reinterpret_cast<const uint4*>(stage + rr * kStageRowBytes + ch * 16);
       if (t0 + rr < query_len) reinterpret_cast<uint4*>(out_head + o_row(t0 + rr))[ch] = w;
     }
+    }
   }
 
   // ---- release TMEM once every warp is done with it
@@ -537,14 +666,17 @@ __global__ void __maxnreg__(96)
 
 cudaError_t run_prefill_attention(const AttentionParams& p, const CUtensorMap& k_map,
                                   const CUtensorMap& v_map, const CUtensorMap* q_map, bool q_ht,
-                                  int dtype, cudaStream_t stream) {
+                                  int dtype, cudaStream_t stream, const PrefillPlan* plan) {
   PrefillKernelParams P;
   P.a = p;
+  P.plan = plan != nullptr ? *plan : PrefillPlan{nullptr, 0, 0, nullptr, nullptr, nullptr};
   P.group = p.num_q_heads / p.num_kv_heads;
   P.q_tma = q_map != nullptr ? 1 : 0;
   P.q_ht = q_ht ? 1 : 0;
-  const dim3 grid(unsigned((p.query_len + kRows - 1) / kRows), unsigned(p.num_q_heads / 2),
-                  unsigned(att_launch_count(p)));
+  const dim3 grid = P.plan.items != nullptr
+                        ? dim3(unsigned(P.plan.num_items), 1u, 1u)
+                        : dim3(unsigned((p.query_len + kRows - 1) / kRows), unsigned(p.num_q_heads / 2),
+                               unsigned(att_launch_count(p)));
   auto launch = [&](auto kernel) {
     cudaError_t e = allow_smem(kernel, kSmemBytes, stream);
     if (e != cudaSuccess) return e;

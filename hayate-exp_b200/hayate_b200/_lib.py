@@ -21,6 +21,7 @@ DEVICE_ERRORS = {
     8: "a bounded pipeline wait gave up",
     16: "tensor-core ops issued on other than exactly one lane (work skipped)",
     32: "packed batch metadata (q_start / q_len / request id) out of range",
+    64: "prefill plan item out of range",
 }
 
 _c_i32, _c_i64, _c_f32, _c_size, _c_p = (ctypes.c_int32, ctypes.c_int64, ctypes.c_float,
@@ -63,6 +64,10 @@ SIGNATURES = {
                                                   _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_f32, _c_p,
                                                   _c_i32, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_p,
                                                   _c_size, _c_p, _c_p]),
+    "hyt_prefill_plan": (_c_i32, [_c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_i32, _c_p]),
+    "hyt_prefill_workspace_bytes": (_c_size, [_c_i32]),
+    "hyt_prefill_attention_planned": (ctypes.c_int, _ATTENTION_ARGS + [_c_p, _c_i32, _c_i32, _c_p, _c_size,
+                                                                       _c_p, _c_p]),
     "hyt_attention_workspace_bytes": (_c_size, [_c_i32] * 8),
     "hyt_workspace_init": (ctypes.c_int, [_c_p, _c_size, _c_p]),
     "hyt_wait_self_test": (ctypes.c_int, [_c_p, _c_p, _c_p]),

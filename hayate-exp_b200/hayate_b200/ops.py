@@ -7,6 +7,7 @@ message if the call is refused. All launches go on the current CUDA stream.
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -386,3 +387,76 @@ def wait_self_test(error_word: torch.Tensor) -> tuple[int, int]:
     _lib.check(rc, "hyt_wait_self_test")
     first, second = elapsed.tolist()
     return first, second
+
+
+# ---------------------------------------------------------------------------- prefill schedule
+def prefill_plan(cache_lens, query_len: int, num_q_heads: int, num_sms: int, max_splits: int = 128,
+                 q_lens=None):
+    """Host-side schedule for the prefill kernel (``hyt_prefill_plan``).
+
+    ``cache_lens`` / ``q_lens`` are host sequences (one entry per request of the launch).
+    Returns ``(items, num_splits)``: ``items`` an int32 ``[n, 4]`` array for
+    ``prefill_attention_planned``, or ``None`` when the default grid is at least as good.
+    """
+    import numpy as np
+
+    lens = np.ascontiguousarray(np.asarray(cache_lens, dtype=np.int32))
+    ql = None if q_lens is None else np.ascontiguousarray(np.asarray(q_lens, dtype=np.int32))
+    batch = lens.size
+    qmax = int(ql.max()) if ql is not None else int(query_len)
+    tiles = sum(-(-int(n) // 128) for n in ql) if ql is not None else batch * -(-qmax // 128)
+    max_items = tiles * (num_q_heads // 2) + max_splits
+    items = np.zeros((max(max_items, 1), 4), dtype=np.int32)
+    splits = ctypes.c_int32(0)
+    n = _lib.lib().hyt_prefill_plan(lens.ctypes.data, None if ql is None else ql.ctypes.data, batch,
+                                    qmax, num_q_heads, num_sms, max_splits, items.ctypes.data,
+                                    max_items, ctypes.byref(splits))
+    if n < 0:
+        _lib.check(n, "hyt_prefill_plan")
+    return (items[:n].copy(), int(splits.value)) if n > 0 else (None, 0)
+
+
+def prefill_workspace_bytes(num_splits: int) -> int:
+    return int(_lib.lib().hyt_prefill_workspace_bytes(num_splits))
+
+
+def prefill_attention_planned(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, layer: int,
+                              page_table: torch.Tensor, cache_lens: torch.Tensor, page_size: int,
+                              items: torch.Tensor | None, num_splits: int,
+                              workspace: torch.Tensor | None = None, scale: float | None = None,
+                              out: torch.Tensor | None = None,
+                              error_word: torch.Tensor | None = None) -> torch.Tensor:
+    """The tcgen05 prefill kernel launched on a plan from ``prefill_plan`` (``items`` an
+    int32 ``[n, 4]`` CUDA tensor; ``None`` runs the default grid)."""
+    _require_cuda(q, k_pool, v_pool, page_table, cache_lens)
+    num_layers, num_kv_heads, capacity, head_dim = _pool_geometry(k_pool, v_pool)
+    batch, num_q_heads, query_len, d = q.shape
+    if d != head_dim or q.dtype != k_pool.dtype:
+        raise ValueError("q must match the pool's head_dim and dtype")
+    if out is None:
+        out = torch.empty((batch, query_len, num_q_heads, head_dim), dtype=q.dtype,
+                          device=q.device).transpose(1, 2)
+    if out.shape != q.shape or out.dtype != q.dtype:
+        raise ValueError("out must match q")
+    n_items = 0
+    if items is not None:
+        _require_cuda(items)
+        if items.dtype != torch.int32 or items.dim() != 2 or items.shape[1] != 4 or not items.is_contiguous():
+            raise ValueError("items must be a contiguous int32 [n, 4] CUDA tensor")
+        n_items = items.shape[0]
+    need = prefill_workspace_bytes(num_splits) if n_items else 0
+    if need and (workspace is None or workspace.numel() < need):
+        raise RuntimeError(f"the plan needs a zeroed workspace of {need} bytes")
+    qs = _lib.int64_array(_bht_strides(q, "q"))
+    os_ = _lib.int64_array(_bht_strides(out, "out"))
+    pts = _table_args(page_table, cache_lens, batch)
+    scale = 1.0 / math.sqrt(head_dim) if scale is None else float(scale)
+    rc = _lib.lib().hyt_prefill_attention_planned(
+        q.data_ptr(), qs, k_pool.data_ptr(), v_pool.data_ptr(), num_layers, layer, capacity,
+        page_table.data_ptr(), pts, cache_lens.data_ptr(), out.data_ptr(), os_, batch, query_len,
+        num_q_heads, num_kv_heads, head_dim, page_size, dtype_code(q.dtype), scale,
+        items.data_ptr() if n_items else None, n_items, num_splits if n_items else 0,
+        _ptr(workspace) if need else None, workspace.numel() if need else 0, _ptr(error_word),
+        _stream_ptr())
+    _lib.check(rc, "hyt_prefill_attention_planned")
+    return out

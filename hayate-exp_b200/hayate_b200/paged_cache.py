@@ -185,10 +185,11 @@ class PagedKVBatch:
     """
 
     __slots__ = ("k_cache", "v_cache", "page_table", "cache_lens", "page_size", "query_len",
-                 "max_kv_len", "cache_lens_i32", "layout", "workspace", "_manager", "_meta")
+                 "max_kv_len", "cache_lens_i32", "layout", "workspace", "_manager", "_meta",
+                 "_host_lens", "_plans")
 
     def __init__(self, manager, page_table, cache_lens, cache_lens_i32, query_len, max_kv_len, meta,
-                 layout: PackedLayout | None = None):
+                 layout: PackedLayout | None = None, host_lens=None):
         self.k_cache = manager.k_cache
         self.v_cache = manager.v_cache
         self.page_table = page_table
@@ -201,6 +202,8 @@ class PagedKVBatch:
         self.workspace = None  # a batch with a fixed workspace (graph replays) sets its own
         self._manager = manager
         self._meta = meta  # keeps the uploaded buffer alive while kernels read it
+        self._host_lens = host_lens  # cache lengths on the host (the prefill schedule's input)
+        self._plans = {}             # num_q_heads -> (plan items on the device or None, splits)
 
     def write_layer(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor) -> None:
         """Scatter the step's new K/V ``[B, H_kv, T, D]`` into this layer's pages."""
@@ -258,6 +261,13 @@ class PagedKVBatch:
                 lay.q_start, lay.q_len, lay.decode_ids, lay.prefill_ids, self.page_size,
                 self.query_len, self.max_kv_len, workspace=workspace, error_word=manager.error_word,
                 split_tokens=manager.split_tokens)
+        planned = self._prefill_schedule(q)
+        if planned is not None:
+            items, splits = planned
+            return ops.prefill_attention_planned(
+                q, self.k_cache, self.v_cache, layer_idx, self.page_table, self.cache_lens_i32,
+                self.page_size, items, splits, workspace=manager.prefill_workspace(splits),
+                error_word=manager.error_word)
         workspace = manager.workspace_for(q.shape[0], self.query_len, q.shape[1], self.max_kv_len)
         return ops.paged_attention(q, self.k_cache, self.v_cache, layer_idx, self.page_table,
                                    self.cache_lens_i32, self.page_size, self.max_kv_len,
@@ -288,6 +298,31 @@ class PagedKVBatch:
                                            self.max_kv_len, workspace=workspace,
                                            error_word=manager.error_word,
                                            split_tokens=manager.split_tokens)
+
+    def _prefill_schedule(self, q: torch.Tensor):
+        """(items, splits) for a planned prefill launch of this batch, or None for the
+        library's own dispatch. The plan (``ops.prefill_plan``: longest items first, the
+        heaviest cut in two) is made on the host once per batch and head count and reused
+        by every layer."""
+        manager = self._manager
+        if (manager.kernel != "auto" or not manager.prefill_plan or self._host_lens is None
+                or q.dtype not in (torch.bfloat16, torch.float16) or q.shape[3] != 128
+                or self.page_size % 128 or q.device.type != "cuda"):
+            return None
+        heads = q.shape[1]
+        group = heads // manager.num_kv_heads
+        if group % 2 or group * self.query_len <= 16:  # the decode kernel's shapes
+            return None
+        if q.data_ptr() % 16 or any(st % 8 for st in q.stride()[:3]):
+            return None
+        if heads not in self._plans:
+            items, splits = ops.prefill_plan(self._host_lens, self.query_len, heads, manager.num_sms,
+                                             manager.prefill_max_splits)
+            if items is not None:
+                items = torch.from_numpy(items).to(q.device, non_blocking=False)
+            self._plans[heads] = (items, splits)
+        items, splits = self._plans[heads]
+        return None if items is None else (items, splits)
 
     def _write_packed(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor) -> None:
         lay = self.layout
@@ -404,6 +439,10 @@ class PagedKVCacheManager:
         self._scratch_page: int | None = None
         self.kernel = "auto"     # pin a kernel ("decode", "prefill", "generic") for testing
         self.split_tokens = 0    # 0 lets the library pick the decode split size
+        self.prefill_plan = True       # schedule prefill launches (longest first, heaviest split)
+        self.prefill_max_splits = 128  # split slots a schedule may use
+        self._prefill_ws = None
+        self._num_sms = None
 
     # ------------------------------------------------------------------ pages
     def _take_pages(self, count: int) -> list[int]:
@@ -619,7 +658,8 @@ class PagedKVCacheManager:
             meta = self._uploader.upload(host)
             table = self._rows.gather(meta[3 * batch:].long(), width)
             return PagedKVBatch(self, table, meta[: 2 * batch].view(torch.int64),
-                                meta[2 * batch: 3 * batch], query_len, max(kv_lengths), (meta, table))
+                                meta[2 * batch: 3 * batch], query_len, max(kv_lengths), (meta, table),
+                                host_lens=list(lengths))
         q_len = np.asarray(query_lens, dtype=np.int32)
         q_start = np.zeros(batch, dtype=np.int32)
         np.cumsum(q_len[:-1], out=q_start[1:])
@@ -684,6 +724,22 @@ class PagedKVCacheManager:
             self._workspace = ops.new_workspace(need, self.device)
         return self._workspace
 
+    @property
+    def num_sms(self) -> int:
+        if getattr(self, "_num_sms", None) is None:
+            self._num_sms = (torch.cuda.get_device_properties(self.device).multi_processor_count
+                             if self.device.type == "cuda" else 1)
+        return self._num_sms
+
+    def prefill_workspace(self, num_splits: int):
+        """Grow-only zeroed workspace for split prefill items (None if the plan has none)."""
+        need = ops.prefill_workspace_bytes(num_splits)
+        if need == 0:
+            return None
+        if self._prefill_ws is None or self._prefill_ws.numel() < need:
+            self._prefill_ws = ops.new_workspace(need, self.device)
+        return self._prefill_ws
+
     def check_device_errors(self) -> None:
         """Synchronise and raise if a kernel refused a page id or length since the last check."""
         problems = ops.read_device_errors(self.error_word)
@@ -691,6 +747,8 @@ class PagedKVCacheManager:
             self.error_word.zero_()
             if self._workspace is not None:
                 self._workspace.zero_()
+            if self._prefill_ws is not None:
+                self._prefill_ws.zero_()
             raise RuntimeError("paged attention kernels refused input: " + "; ".join(problems))
 
     def _physical_positions(self, handle: PagedCacheHandle, length: int) -> torch.Tensor:

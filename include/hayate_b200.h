@@ -53,7 +53,8 @@ enum {
   HYT_DEVERR_SPLIT_RANGE = 4,  /* kv_len > max_kv_len given at launch */
   HYT_DEVERR_WAIT_TIMEOUT = 8, /* a bounded pipeline wait gave up */
   HYT_DEVERR_ISSUE_LANE = 16,  /* tensor-core issue ran on other than exactly one lane (work skipped) */
-  HYT_DEVERR_PACKED_RANGE = 32 /* packed batch: q_start/q_len/request id out of range (work skipped) */
+  HYT_DEVERR_PACKED_RANGE = 32, /* packed batch: q_start/q_len/request id out of range (work skipped) */
+  HYT_DEVERR_PLAN_RANGE = 64    /* prefill plan item out of range (work skipped) */
 };
 
 /* Message of the last failed call on this thread ("" if none). */
@@ -255,6 +256,41 @@ int hyt_paged_attention_packed(const void* q, const int64_t* q_strides, const vo
                                int32_t max_query_len, int32_t max_kv_len, int32_t split_tokens,
                                void* workspace, size_t workspace_bytes, int32_t* error_word,
                                void* stream);
+
+/*
+ * Prefill schedule (host function, no GPU): the order in which the tcgen05 prefill
+ * kernel's work items (query tile, head pair, request) start, and which of the heaviest
+ * are cut in two along their keys (the halves merged by whichever finishes second), so
+ * that the last wave of CTAs ends evenly. Replaces nothing in hayate (its FlexAttention
+ * grid is fixed); a planned launch computes the same rows as hyt_prefill_attention.
+ * cache_lens / q_lens are HOST arrays (q_lens NULL: every request has query_len queries).
+ * The plan is chosen by simulating the block scheduler on num_sms SMs for the default
+ * grid and for longest-first orders with 0..max_splits items cut; items (4 int32 each,
+ * room for max_items) receives it. Returns the number of items, 0 when the default grid
+ * is at least as good (launch without a plan), negative on bad arguments.
+ * *num_splits receives the number of split slots the plan uses.
+ */
+int32_t hyt_prefill_plan(const int32_t* cache_lens, const int32_t* q_lens, int32_t batch,
+                         int32_t query_len, int32_t num_q_heads, int32_t num_sms,
+                         int32_t max_splits, int32_t* items, int32_t max_items,
+                         int32_t* num_splits);
+
+/* Workspace bytes a plan with num_splits split slots needs (its counters must be zero
+ * before first use, hyt_workspace_init; the kernel leaves them zero). */
+size_t hyt_prefill_workspace_bytes(int32_t num_splits);
+
+/* hyt_prefill_attention launched on a plan from hyt_prefill_plan: items is the plan in
+ * DEVICE memory (num_items entries of 4 int32; num_items 0 = the default grid). */
+int hyt_prefill_attention_planned(const void* q, const int64_t* q_strides, const void* k_pool,
+                                  const void* v_pool, int32_t num_layers, int32_t layer,
+                                  int64_t capacity_tokens, const int32_t* page_table,
+                                  int32_t page_table_stride, const int32_t* cache_lens, void* out,
+                                  const int64_t* out_strides, int32_t batch, int32_t query_len,
+                                  int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                  int32_t page_size, int32_t dtype, float scale,
+                                  const int32_t* items, int32_t num_items, int32_t num_splits,
+                                  void* workspace, size_t workspace_bytes, int32_t* error_word,
+                                  void* stream);
 
 /* Workspace bytes hyt_paged_attention / hyt_decode_attention need for these sizes
  * (0 when the dispatched kernel needs none). split_tokens as in the call. */

@@ -1,0 +1,104 @@
+"""Planned prefill launches (longest items first, the heaviest cut in two and merged).
+
+A planned launch must produce the rows of the default grid (within the bf16/f16
+tolerance of 2e-2: a split item's halves are merged in f32 in another order) and of the
+oracle; the same plan launched again (one per layer) gives identical rows and leaves the
+split counters zero; a refused page in a split item is flagged and the next call is clean.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from hayate_b200 import PagedKVCacheManager, ops
+from hayate_b200 import workloads as W
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def build(lengths, query_len, dtype=torch.bfloat16, seed=0):
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    pages = sum(math.ceil((n + query_len) / 128) for n in lengths) + 2
+    m = PagedKVCacheManager(1, 8, 128, pages * 128, 128, len(lengths), dtype, "cuda")
+    W.shuffle_free_pages(m, seed)
+    hs = [m.allocate() for _ in lengths]
+    for h, n in zip(hs, lengths):
+        W.fill_history(m, h, n, gen)
+    q, k, v = W.step_inputs(m, hs, query_len, 32, gen)
+    batch = m.begin_batch(hs, query_len)
+    batch.write_layer(0, k, v)
+    return m, hs, batch, q
+
+
+def oracle_rows(m, batch, q, requests=None):
+    return oracle.paged_attention(q.float().cpu().numpy(), m.k_cache.float().cpu().numpy(),
+                                  m.v_cache.float().cpu().numpy(), 0,
+                                  batch.page_table.cpu().numpy().astype(np.int64),
+                                  batch.cache_lens.cpu().numpy(), m.page_size, requests=requests)
+
+
+CASES = [
+    ([2998, 4045, 1590, 2020, 1436, 3762, 183, 2532], 512),   # config 3
+    ([1100, 516, 2089, 965, 4058, 3682, 3868, 3109], 512),
+    ([0, 9000], 300),
+    ([40], 40),
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=str)
+@pytest.mark.parametrize("lengths, query_len", CASES, ids=str)
+def test_planned_prefill_matches_default_grid_and_oracle(lengths, query_len, dtype):
+    m, hs, batch, q = build(lengths, query_len, dtype, seed=len(lengths) + query_len)
+    planned = batch._prefill_schedule(q)
+    out = batch.attend_layer(q, 0)
+    m.prefill_plan = False
+    ref = m.begin_batch(hs, query_len).attend_layer(q, 0)
+    torch.cuda.synchronize()
+    m.check_device_errors()
+    assert (out.float() - ref.float()).abs().max().item() <= 2e-2
+    sample = list(range(min(2, len(lengths))))
+    err = np.abs(out.float().cpu().numpy()[sample] - oracle_rows(m, batch, q, sample)[sample]).max()
+    assert err <= 2e-2, err
+    if planned is not None:  # a split plan really ran (config 3 splits items)
+        items, splits = planned
+        assert items.shape[1] == 4
+        if splits:
+            ws = m.prefill_workspace(splits)
+            assert int(ws[: 4 * splits].view(torch.int32).abs().sum().item()) == 0
+
+
+def test_plan_is_used_on_config3_and_is_deterministic():
+    lengths, query_len = CASES[0]
+    m, hs, batch, q = build(lengths, query_len, seed=3)
+    planned = batch._prefill_schedule(q)
+    assert planned is not None and planned[1] > 0  # this batch gets split items
+    outs = [batch.attend_layer(q, 0) for _ in range(4)]  # one plan, several layers
+    torch.cuda.synchronize()
+    m.check_device_errors()
+    assert all(torch.equal(outs[0], o) for o in outs[1:])
+
+
+def test_planned_prefill_refused_page_then_clean_call():
+    lengths, query_len = CASES[0]
+    m, hs, batch, q = build(lengths, query_len, seed=5)
+    items, splits = batch._prefill_schedule(q)
+    table = batch.page_table.clone()
+    table[1, 3] = m.num_pages + 1  # request 1 (prefix 4045): its heaviest items are split
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ws = m.prefill_workspace(splits)
+    ops.prefill_attention_planned(q, m.k_cache, m.v_cache, 0, table, batch.cache_lens_i32, 128, items,
+                                  splits, workspace=ws, error_word=err)
+    torch.cuda.synchronize()
+    assert "page id outside the pool" in ops.read_device_errors(err)
+    assert int(ws[: 4 * splits].view(torch.int32).abs().sum().item()) == 0  # counters reset
+    out = batch.attend_layer(q, 0)
+    torch.cuda.synchronize()
+    m.check_device_errors()
+    err2 = np.abs(out.float().cpu().numpy()[[1]] - oracle_rows(m, batch, q, [1])[[1]]).max()
+    assert err2 <= 2e-2, err2
