@@ -59,6 +59,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="headline workload only")
+    ap.add_argument("--no-prefill-plan", action="store_true",
+                    help="prefill on the default grid instead of the planned schedule")
     ap.add_argument("--prefix-max", type=int, default=4096,
                     help="prefill workload: prefixes drawn from U[0, prefix-max] (config 3: 4096)")
     ap.add_argument("--reference-gpu", action="store_true",
@@ -522,19 +524,17 @@ def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=N
     for h, n in zip(handles, prefixes):
         W.fill_history(manager, h, n, gen)
     q, k, v = W.step_inputs(manager, handles, T, 32, gen)
+    manager.prefill_plan = not args.no_prefill_plan
     batch = manager.begin_batch(handles, T)
-    out = torch.empty((len(prefixes), T, 32, 128), dtype=q.dtype, device="cuda").transpose(1, 2)
     flops = attention_flops(prefixes, T, 32, 128)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")  # > 126 MB L2
 
     def step(ev=None):
-        ops.kv_scatter(k, v, manager.k_cache, manager.v_cache, 0, batch.page_table,
-                       batch.cache_lens_i32, 128, error_word=manager.error_word)
+        """write_layer + attend_layer of one layer through the public API."""
+        batch.write_layer(0, k, v)
         if ev is not None:
             ev[1].record()
-        ops.paged_attention(q, manager.k_cache, manager.v_cache, 0, batch.page_table,
-                            batch.cache_lens_i32, 128, batch.max_kv_len, out=out,
-                            error_word=manager.error_word)
+        return batch.attend_layer(q, 0)
 
     for _ in range(warmup):
         step()
@@ -552,6 +552,10 @@ def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=N
         torch.cuda.synchronize()
         barrier(world)
     manager.check_device_errors()
+    out = step()  # the rows (compared with the reference's when --reference-gpu)
+    plan = batch._prefill_schedule(q)
+    schedule = ("default grid" if plan is None else
+                f"planned: {plan[0].shape[0]} CTAs, {plan[1]} items cut in two (longest first)")
     step_ms = sum(a.elapsed_time(c) for a, _, c in evs) / steps
     attn_ms = sum(b.elapsed_time(c) for _, b, c in evs) / steps
     step_ms = max_over_ranks(step_ms, world)
@@ -579,6 +583,7 @@ def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=N
                      "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + write.sum)",
                      "kernel": "prefill_attention_kernel (tcgen05 + TMEM)"},
         "l2": "256 MB buffer written between timed steps (L2 flush); events bracket each step",
+        "schedule": schedule,
         "gpu_launches": 2 * steps,
         "clocks": clocks.summary(),
     }
