@@ -281,8 +281,11 @@ class PagedKVBatch:
         same pool bytes and rows. A decode step runs as one launch: the decode kernel writes
         the new K/V rows itself before reading them."""
         manager = self._manager
-        if self.layout is not None or manager.kernel != "auto":
-            self.write_layer(layer_idx, k, v)
+        decode_step = (q.dtype in (torch.bfloat16, torch.float16) and q.shape[-1] == 128
+                       and self.page_size % 64 == 0
+                       and (q.shape[1] // manager.num_kv_heads) * self.query_len <= 16)
+        if self.layout is not None or manager.kernel != "auto" or not decode_step:
+            self.write_layer(layer_idx, k, v)  # the two kernels in turn (prefill: its schedule)
             return self.attend_layer(q, layer_idx)
         if k.shape[2] != self.query_len or v.shape != k.shape:
             raise ValueError("k and v must be [batch, kv_heads, query_len, head_dim]")
