@@ -456,11 +456,13 @@ int launch_generic(const void* q, const int64_t* qs, const void* k_pool, const v
 }
 
 // ------------------------------------------------------------------ prefill schedule
-// Cost model of one prefill work item, in key tiles: the tiles it streams plus a fixed
-// start-up/epilogue cost; a half of a split item pays the start-up again and its share of
-// the merge. Measured per CTA on config 3: ~2 us per key tile, ~5 us of start-up and
-// epilogue.
-constexpr double kItemOverhead = 2.5, kMergeCost = 0.5;
+// Cost model of one prefill work item, in key tiles (~2 us each on a B200): the tiles it
+// streams plus a fixed start-up/epilogue cost; a half of a split item pays the start-up
+// again plus the merge (its partial out to the workspace, both read back by the second
+// half). The two constants are fitted to B200 timings of the default grid, longest-first
+// orders and split plans on four prefix sets (config 3, two random U[0, 4096] sets and
+// U[0, 32768]); a plan is used only when the model predicts it at least kMinGain faster.
+constexpr double kItemOverhead = 5.0, kMergeCost = 8.0, kMinGain = 0.03;
 
 struct PlanEntry {
   int32_t z, q_tile, pair, k_lo, k_hi, split;  // split: slot * 2 + part, or -1
@@ -1018,7 +1020,8 @@ int32_t hyt_prefill_plan(const int32_t* cache_lens, const int32_t* q_lens, int32
   if (base.empty()) return 0;
   std::vector<double> costs;
   for (const PlanEntry& e : base) costs.push_back(e.cost);
-  double best = greedy_makespan(costs, num_sms);  // the default grid
+  const double grid = greedy_makespan(costs, num_sms);  // the default grid
+  double best = grid;
   int best_k = -1;
   // longest first, the k heaviest items cut in two along their keys
   std::vector<PlanEntry> lpt = base;
@@ -1057,7 +1060,7 @@ int32_t hyt_prefill_plan(const int32_t* cache_lens, const int32_t* q_lens, int32
       best_k = k;
     }
   }
-  if (best_k < 0) return 0;  // the default grid is as good: no plan
+  if (best_k < 0 || best > (1.0 - kMinGain) * grid) return 0;  // the default grid: no plan
   build(best_k, &cand);
   for (size_t i = 0; i < cand.size(); ++i) {
     const PlanEntry& e = cand[i];

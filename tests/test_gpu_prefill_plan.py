@@ -44,11 +44,13 @@ def oracle_rows(m, batch, q, requests=None):
 
 
 CASES = [
-    ([2998, 4045, 1590, 2020, 1436, 3762, 183, 2532], 512),   # config 3
-    ([1100, 516, 2089, 965, 4058, 3682, 3868, 3109], 512),
-    ([0, 9000], 300),
+    ([2998, 4045, 1590, 2020, 1436, 3762, 183, 2532], 512),   # config 3: the default grid
+    ([1100, 516, 2089, 965, 4058, 3682, 3868, 3109], 512),    # longest first, no split
+    ([0, 9000], 300),                                          # split items
+    ([20000], 512),                                            # split items
     ([40], 40),
 ]
+SPLIT = ([0, 9000], 300)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=str)
@@ -73,8 +75,23 @@ def test_planned_prefill_matches_default_grid_and_oracle(lengths, query_len, dty
             assert int(ws[: 4 * splits].view(torch.int32).abs().sum().item()) == 0
 
 
-def test_plan_is_used_on_config3_and_is_deterministic():
-    lengths, query_len = CASES[0]
+def test_plan_choices():
+    """Config 3 keeps the default grid, a U[0, 4096] batch it does not suit is reordered,
+    and few long items are cut in two."""
+    assert batch_plan(*CASES[0]) is None
+    items, splits = batch_plan(*CASES[1])
+    assert items.shape[0] == 8 * 4 * 16 and splits == 0
+    items, splits = batch_plan(*SPLIT)
+    assert splits > 0
+
+
+def batch_plan(lengths, query_len):
+    m, hs, batch, q = build(lengths, query_len, seed=1)
+    return batch._prefill_schedule(q)
+
+
+def test_split_plan_is_deterministic():
+    lengths, query_len = SPLIT
     m, hs, batch, q = build(lengths, query_len, seed=3)
     planned = batch._prefill_schedule(q)
     assert planned is not None and planned[1] > 0  # this batch gets split items
@@ -85,11 +102,12 @@ def test_plan_is_used_on_config3_and_is_deterministic():
 
 
 def test_planned_prefill_refused_page_then_clean_call():
-    lengths, query_len = CASES[0]
+    lengths, query_len = SPLIT
     m, hs, batch, q = build(lengths, query_len, seed=5)
     items, splits = batch._prefill_schedule(q)
+    assert splits > 0
     table = batch.page_table.clone()
-    table[1, 3] = m.num_pages + 1  # request 1 (prefix 4045): its heaviest items are split
+    table[1, 3] = m.num_pages + 1  # request 1 (prefix 9000): its items are the split ones
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     ws = m.prefill_workspace(splits)
     ops.prefill_attention_planned(q, m.k_cache, m.v_cache, 0, table, batch.cache_lens_i32, 128, items,

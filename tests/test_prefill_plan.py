@@ -54,8 +54,9 @@ def test_plan_covers_every_item_once(seed):
         return
     check_cover(items, splits, cache_lens, q_lens, 32)
     assert splits <= 128
-    # longest first: the halves and whole items in non-increasing cost order
-    costs = [((k >> 16) - (k & 0xFFFF)) + (0.5 if s >= 0 else 0.0) for _, _, k, s in items.tolist()]
+    # longest first: the halves (which also pay the merge, 8 key tiles in the cost model)
+    # and whole items in non-increasing cost order
+    costs = [((k >> 16) - (k & 0xFFFF)) + (8.0 if s >= 0 else 0.0) for _, _, k, s in items.tolist()]
     assert all(a >= b - 1e-9 for a, b in zip(costs, costs[1:]))
 
 
