@@ -67,7 +67,7 @@ def test_planned_prefill_matches_default_grid_and_oracle(lengths, query_len, dty
     sample = list(range(min(2, len(lengths))))
     err = np.abs(out.float().cpu().numpy()[sample] - oracle_rows(m, batch, q, sample)[sample]).max()
     assert err <= 2e-2, err
-    if planned is not None:  # a split plan really ran (config 3 splits items)
+    if planned is not None:  # a planned launch ran: its split counters are back at zero
         items, splits = planned
         assert items.shape[1] == 4
         if splits:
