@@ -45,6 +45,13 @@
 // shared token axis; query tiles past a request's chunk exit at once, and a request
 // list (req_ids) picks the requests the launch serves.
 //
+// Planned launches (PrefillPlan, made on the host by hyt_prefill_plan): a 1-D grid whose
+// CTA i takes item i of the plan (request, query tile, head pair, key-tile range), so
+// that the longest items start first. An item cut in two runs as two CTAs over the two
+// halves of its key tiles; each writes its partial (unnormalised O, running max, sum)
+// to its slot of the split workspace and the second to arrive merges both (the same
+// online-softmax merge as across tiles) and resets the slot's counter.
+//
 // FLOPs per launch counted by the roofline: 4 * H_q * 128 per causal-valid
 // (query, key) pair.
 #include <type_traits>
