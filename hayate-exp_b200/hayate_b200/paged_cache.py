@@ -321,8 +321,8 @@ class PagedKVBatch:
         if heads not in self._plans:
             items, splits = ops.prefill_plan(self._host_lens, self.query_len, heads, manager.num_sms,
                                              manager.prefill_max_splits)
-            if items is not None:
-                items = torch.from_numpy(items).to(q.device, non_blocking=False)
+            if items is not None:  # one pinned asynchronous upload per batch
+                items = manager._uploader.upload(items.reshape(-1)).view(-1, 4)
             self._plans[heads] = (items, splits)
         items, splits = self._plans[heads]
         return None if items is None else (items, splits)
