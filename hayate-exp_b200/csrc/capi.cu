@@ -945,20 +945,19 @@ int hyt_norm_rope_scatter_packed(const void* q, const void* k, const void* v,
   return HYT_OK;
 }
 
-int hyt_paged_attention_packed(const void* q, const int64_t* q_strides, const void* k_pool,
-                               const void* v_pool, int32_t num_layers, int32_t layer,
-                               int64_t capacity_tokens, const int32_t* page_table,
-                               int32_t page_table_stride, const int32_t* cache_lens,
-                               const int32_t* q_start, const int32_t* q_len, void* out,
-                               const int64_t* out_strides, int32_t batch, int32_t total_tokens,
-                               int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
-                               int32_t page_size, int32_t dtype, float scale,
-                               const int32_t* decode_ids, int32_t num_decode,
-                               const int32_t* prefill_ids, int32_t num_prefill,
-                               int32_t max_query_len, int32_t max_kv_len, int32_t split_tokens,
-                               void* workspace, size_t workspace_bytes, int32_t* error_word,
-                               void* stream) {
-  g_last_error.clear();
+static int packed_attention(const void* q, const int64_t* q_strides, const void* k_pool,
+                            const void* v_pool, int32_t num_layers, int32_t layer,
+                            int64_t capacity_tokens, const int32_t* page_table,
+                            int32_t page_table_stride, const int32_t* cache_lens,
+                            const int32_t* q_start, const int32_t* q_len, void* out,
+                            const int64_t* out_strides, int32_t batch, int32_t total_tokens,
+                            int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                            int32_t page_size, int32_t dtype, float scale,
+                            const int32_t* decode_ids, int32_t num_decode,
+                            const int32_t* prefill_ids, int32_t num_prefill,
+                            int32_t max_query_len, int32_t max_kv_len, int32_t split_tokens,
+                            void* workspace, size_t workspace_bytes, int32_t* error_word,
+                            void* stream, const hyt::PrefillPlan* plan) {
   if (!q || !q_strides || !k_pool || !v_pool || !page_table || !cache_lens || !q_start ||
       !q_len || !out || !out_strides)
     return fail(HYT_ERR_INVALID, "null pointer argument");
@@ -996,12 +995,75 @@ int hyt_paged_attention_packed(const void* q, const int64_t* q_strides, const vo
     const PackedArgs pk{q_start, q_len, prefill_ids, num_prefill, total_tokens};
     if (prefill_eligible(g, q, qs, out, os))
       rc = launch_prefill(q, qs, k_pool, v_pool, g, page_table, cache_lens, out, os, scale,
-                          error_word, st, &pk);
+                          error_word, st, &pk, plan);
+    else if (plan != nullptr)
+      rc = fail(HYT_ERR_UNSUPPORTED, "a prefill plan needs the tcgen05 prefill kernel's shapes");
     else
       rc = launch_generic(q, qs, k_pool, v_pool, g, page_table, cache_lens, out, os, scale,
                           error_word, st, &pk);
   }
   return rc;
+}
+
+int hyt_paged_attention_packed(const void* q, const int64_t* q_strides, const void* k_pool,
+                               const void* v_pool, int32_t num_layers, int32_t layer,
+                               int64_t capacity_tokens, const int32_t* page_table,
+                               int32_t page_table_stride, const int32_t* cache_lens,
+                               const int32_t* q_start, const int32_t* q_len, void* out,
+                               const int64_t* out_strides, int32_t batch, int32_t total_tokens,
+                               int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                               int32_t page_size, int32_t dtype, float scale,
+                               const int32_t* decode_ids, int32_t num_decode,
+                               const int32_t* prefill_ids, int32_t num_prefill,
+                               int32_t max_query_len, int32_t max_kv_len, int32_t split_tokens,
+                               void* workspace, size_t workspace_bytes, int32_t* error_word,
+                               void* stream) {
+  g_last_error.clear();
+  return packed_attention(q, q_strides, k_pool, v_pool, num_layers, layer, capacity_tokens,
+                          page_table, page_table_stride, cache_lens, q_start, q_len, out,
+                          out_strides, batch, total_tokens, num_q_heads, num_kv_heads, head_dim,
+                          page_size, dtype, scale, decode_ids, num_decode, prefill_ids,
+                          num_prefill, max_query_len, max_kv_len, split_tokens, workspace,
+                          workspace_bytes, error_word, stream, nullptr);
+}
+
+static size_t prefill_counter_bytes(int32_t num_splits);
+
+int hyt_paged_attention_packed_planned(
+    const void* q, const int64_t* q_strides, const void* k_pool, const void* v_pool,
+    int32_t num_layers, int32_t layer, int64_t capacity_tokens, const int32_t* page_table,
+    int32_t page_table_stride, const int32_t* cache_lens, const int32_t* q_start,
+    const int32_t* q_len, void* out, const int64_t* out_strides, int32_t batch,
+    int32_t total_tokens, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+    int32_t page_size, int32_t dtype, float scale, const int32_t* decode_ids, int32_t num_decode,
+    const int32_t* prefill_ids, int32_t num_prefill, int32_t max_query_len, int32_t max_kv_len,
+    int32_t split_tokens, void* workspace, size_t workspace_bytes, const int32_t* items,
+    int32_t num_items, int32_t num_splits, void* plan_workspace, size_t plan_workspace_bytes,
+    int32_t* error_word, void* stream) {
+  g_last_error.clear();
+  if (num_items < 0 || num_splits < 0 || (num_items > 0 && items == nullptr))
+    return fail(HYT_ERR_INVALID, "bad plan");
+  if (num_items > 0 && num_splits > 0 &&
+      (plan_workspace == nullptr || plan_workspace_bytes < hyt_prefill_workspace_bytes(num_splits)))
+    return fail(HYT_ERR_WORKSPACE, "plan workspace missing or smaller than hyt_prefill_workspace_bytes()");
+  hyt::PrefillPlan plan{nullptr, 0, 0, nullptr, nullptr, nullptr};
+  if (num_items > 0) {
+    uint8_t* ws = static_cast<uint8_t*>(plan_workspace);
+    const size_t cb = num_splits > 0 ? prefill_counter_bytes(num_splits) : 0;
+    const size_t ml_bytes = size_t(num_splits) * 2 * 2 * 128 * 2 * 4;
+    plan.items = reinterpret_cast<const hyt::PrefillItem*>(items);
+    plan.num_items = num_items;
+    plan.num_splits = num_splits;
+    plan.ws_counter = num_splits > 0 ? reinterpret_cast<int32_t*>(ws) : nullptr;
+    plan.ws_ml = num_splits > 0 ? reinterpret_cast<float*>(ws + cb) : nullptr;
+    plan.ws_o = num_splits > 0 ? reinterpret_cast<float*>(ws + cb + ml_bytes) : nullptr;
+  }
+  return packed_attention(q, q_strides, k_pool, v_pool, num_layers, layer, capacity_tokens,
+                          page_table, page_table_stride, cache_lens, q_start, q_len, out,
+                          out_strides, batch, total_tokens, num_q_heads, num_kv_heads, head_dim,
+                          page_size, dtype, scale, decode_ids, num_decode, prefill_ids,
+                          num_prefill, max_query_len, max_kv_len, split_tokens, workspace,
+                          workspace_bytes, error_word, stream, num_items > 0 ? &plan : nullptr);
 }
 
 int32_t hyt_prefill_plan(const int32_t* cache_lens, const int32_t* q_lens, int32_t batch,

@@ -68,6 +68,13 @@ SIGNATURES = {
     "hyt_prefill_workspace_bytes": (_c_size, [_c_i32]),
     "hyt_prefill_attention_planned": (ctypes.c_int, _ATTENTION_ARGS + [_c_p, _c_i32, _c_i32, _c_p, _c_size,
                                                                        _c_p, _c_p]),
+    "hyt_paged_attention_packed_planned": (ctypes.c_int, [_c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i64,
+                                                          _c_p, _c_i32, _c_p, _c_p, _c_p, _c_p, _c_p,
+                                                          _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
+                                                          _c_i32, _c_i32, _c_f32, _c_p, _c_i32, _c_p,
+                                                          _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_size,
+                                                          _c_p, _c_i32, _c_i32, _c_p, _c_size, _c_p,
+                                                          _c_p]),
     "hyt_attention_workspace_bytes": (_c_size, [_c_i32] * 8),
     "hyt_workspace_init": (ctypes.c_int, [_c_p, _c_size, _c_p]),
     "hyt_wait_self_test": (ctypes.c_int, [_c_p, _c_p, _c_p]),

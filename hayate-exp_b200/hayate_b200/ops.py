@@ -330,10 +330,14 @@ def paged_attention_packed(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.
                            page_size: int, max_query_len: int, max_kv_len: int,
                            scale: float | None = None, out: torch.Tensor | None = None,
                            workspace: torch.Tensor | None = None,
-                           error_word: torch.Tensor | None = None, split_tokens: int = 0) -> torch.Tensor:
+                           error_word: torch.Tensor | None = None, split_tokens: int = 0,
+                           plan_items: torch.Tensor | None = None, plan_splits: int = 0,
+                           plan_workspace: torch.Tensor | None = None) -> torch.Tensor:
     """Causal GQA attention of a packed batch ``q`` ``[1, H_q, N, D]``: the requests in
     ``decode_ids`` (one query each) on the decode kernel, those in ``prefill_ids`` on the
-    prefill kernel, in one call."""
+    prefill kernel, in one call. ``plan_items`` (int32 ``[n, 4]`` CUDA, from
+    ``prefill_plan`` over the prefill requests in ``prefill_ids`` order) schedules the
+    prefill launch."""
     _require_cuda(q, k_pool, v_pool, page_table, cache_lens, q_start, q_len, decode_ids, prefill_ids)
     _int32_cuda(q_start, q_len, decode_ids, prefill_ids)
     num_layers, num_kv_heads, capacity, head_dim = _pool_geometry(k_pool, v_pool)
@@ -354,15 +358,28 @@ def paged_attention_packed(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.
                                      q.dtype, split_tokens) if n_dec else 0
     if need and (workspace is None or workspace.numel() < need):
         raise RuntimeError(f"attention needs a zeroed workspace of {need} bytes")
-    rc = _lib.lib().hyt_paged_attention_packed(
-        q.data_ptr(), qs, k_pool.data_ptr(), v_pool.data_ptr(), num_layers, layer, capacity,
-        page_table.data_ptr(), pts, cache_lens.data_ptr(), q_start.data_ptr(), q_len.data_ptr(),
-        out.data_ptr(), os_, batch, total, num_q_heads, num_kv_heads, head_dim, page_size,
-        dtype_code(q.dtype), scale, decode_ids.data_ptr() if n_dec else None, n_dec,
-        prefill_ids.data_ptr() if n_pre else None, n_pre, max_query_len, max_kv_len, split_tokens,
-        _ptr(workspace) if need else None, workspace.numel() if need else 0, _ptr(error_word),
-        _stream_ptr())
-    _lib.check(rc, "hyt_paged_attention_packed")
+    common = (q.data_ptr(), qs, k_pool.data_ptr(), v_pool.data_ptr(), num_layers, layer, capacity,
+              page_table.data_ptr(), pts, cache_lens.data_ptr(), q_start.data_ptr(), q_len.data_ptr(),
+              out.data_ptr(), os_, batch, total, num_q_heads, num_kv_heads, head_dim, page_size,
+              dtype_code(q.dtype), scale, decode_ids.data_ptr() if n_dec else None, n_dec,
+              prefill_ids.data_ptr() if n_pre else None, n_pre, max_query_len, max_kv_len,
+              split_tokens, _ptr(workspace) if need else None, workspace.numel() if need else 0)
+    if plan_items is None:
+        rc = _lib.lib().hyt_paged_attention_packed(*common, _ptr(error_word), _stream_ptr())
+        _lib.check(rc, "hyt_paged_attention_packed")
+        return out
+    _require_cuda(plan_items)
+    if plan_items.dtype != torch.int32 or plan_items.dim() != 2 or plan_items.shape[1] != 4 \
+            or not plan_items.is_contiguous():
+        raise ValueError("plan_items must be a contiguous int32 [n, 4] CUDA tensor")
+    pneed = prefill_workspace_bytes(plan_splits)
+    if pneed and (plan_workspace is None or plan_workspace.numel() < pneed):
+        raise RuntimeError(f"the plan needs a zeroed workspace of {pneed} bytes")
+    rc = _lib.lib().hyt_paged_attention_packed_planned(
+        *common, plan_items.data_ptr(), plan_items.shape[0], plan_splits,
+        _ptr(plan_workspace) if pneed else None, plan_workspace.numel() if pneed else 0,
+        _ptr(error_word), _stream_ptr())
+    _lib.check(rc, "hyt_paged_attention_packed_planned")
     return out
 
 

@@ -256,11 +256,14 @@ class PagedKVBatch:
             workspace = self.workspace
             if workspace is None and n_dec:
                 workspace = manager.workspace_for(n_dec, 1, q.shape[1], self.max_kv_len)
+            planned = self._prefill_schedule(q)
+            items, splits = planned if planned is not None else (None, 0)
             return ops.paged_attention_packed(
                 q, self.k_cache, self.v_cache, layer_idx, self.page_table, self.cache_lens_i32,
                 lay.q_start, lay.q_len, lay.decode_ids, lay.prefill_ids, self.page_size,
                 self.query_len, self.max_kv_len, workspace=workspace, error_word=manager.error_word,
-                split_tokens=manager.split_tokens)
+                split_tokens=manager.split_tokens, plan_items=items, plan_splits=splits,
+                plan_workspace=manager.prefill_workspace(splits) if items is not None else None)
         planned = self._prefill_schedule(q)
         if planned is not None:
             items, splits = planned
@@ -314,13 +317,22 @@ class PagedKVBatch:
             return None
         heads = q.shape[1]
         group = heads // manager.num_kv_heads
-        if group % 2 or group * self.query_len <= 16:  # the decode kernel's shapes
+        if q.data_ptr() % 16 or any(st % 8 for st in q.stride()[:3]) or group % 2:
             return None
-        if q.data_ptr() % 16 or any(st % 8 for st in q.stride()[:3]):
-            return None
+        lay = self.layout
+        if lay is None:
+            if group * self.query_len <= 16:  # the decode kernel's shapes
+                return None
+            lens, q_lens = self._host_lens, None
+        else:  # the packed batch's prefill requests, in prefill_ids order
+            ids = [i for i, t in enumerate(lay.query_lens) if t > 1]
+            if not ids:
+                return None
+            lens = [self._host_lens[i] for i in ids]
+            q_lens = [lay.query_lens[i] for i in ids]
         if heads not in self._plans:
-            items, splits = ops.prefill_plan(self._host_lens, self.query_len, heads, manager.num_sms,
-                                             manager.prefill_max_splits)
+            items, splits = ops.prefill_plan(lens, self.query_len, heads, manager.num_sms,
+                                             manager.prefill_max_splits, q_lens=q_lens)
             if items is not None:  # one pinned asynchronous upload per batch
                 items = manager._uploader.upload(items.reshape(-1)).view(-1, 4)
             self._plans[heads] = (items, splits)
@@ -684,7 +696,8 @@ class PagedKVCacheManager:
                               prefill_ids=meta[o + 2 * batch + n_dec: o + 3 * batch],
                               token_request=meta[o + 3 * batch:])
         return PagedKVBatch(self, table, meta[: 2 * batch].view(torch.int64), meta[2 * batch: 3 * batch],
-                            max(query_lens), max(kv_lengths), (meta, table), layout)
+                            max(query_lens), max(kv_lengths), (meta, table), layout,
+                            host_lens=list(lengths))
 
     def commit_batch(self, handles: Sequence[PagedCacheHandle], query_len: int | Sequence[int]) -> None:
         """Advance logical lengths after every layer wrote the step's K/V."""

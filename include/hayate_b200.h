@@ -292,6 +292,22 @@ int hyt_prefill_attention_planned(const void* q, const int64_t* q_strides, const
                                   void* workspace, size_t workspace_bytes, int32_t* error_word,
                                   void* stream);
 
+/* hyt_paged_attention_packed with its prefill launch on a plan from hyt_prefill_plan (made
+ * with the prefill requests' cache lengths and chunk lengths, in prefill_ids order: an
+ * item's request index is a position in prefill_ids); items in DEVICE memory, num_items 0
+ * = the default grid; plan_workspace as for hyt_prefill_attention_planned. */
+int hyt_paged_attention_packed_planned(
+    const void* q, const int64_t* q_strides, const void* k_pool, const void* v_pool,
+    int32_t num_layers, int32_t layer, int64_t capacity_tokens, const int32_t* page_table,
+    int32_t page_table_stride, const int32_t* cache_lens, const int32_t* q_start,
+    const int32_t* q_len, void* out, const int64_t* out_strides, int32_t batch,
+    int32_t total_tokens, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+    int32_t page_size, int32_t dtype, float scale, const int32_t* decode_ids, int32_t num_decode,
+    const int32_t* prefill_ids, int32_t num_prefill, int32_t max_query_len, int32_t max_kv_len,
+    int32_t split_tokens, void* workspace, size_t workspace_bytes, const int32_t* items,
+    int32_t num_items, int32_t num_splits, void* plan_workspace, size_t plan_workspace_bytes,
+    int32_t* error_word, void* stream);
+
 /* Workspace bytes hyt_paged_attention / hyt_decode_attention need for these sizes
  * (0 when the dispatched kernel needs none). split_tokens as in the call. */
 size_t hyt_attention_workspace_bytes(int32_t batch, int32_t query_len, int32_t num_q_heads,

@@ -33,6 +33,7 @@ def twin_managers(lengths, query_lens, dtype, seed, page_size=128):
         gen = torch.Generator(device="cuda").manual_seed(seed)
         m = PagedKVCacheManager(1, 8, 128, pages * page_size, page_size, len(lengths), dtype, "cuda")
         m.split_tokens = 256
+        m.prefill_plan = False  # the default grid: bit-exact with the per-request launches
         W.shuffle_free_pages(m, seed)
         hs = [m.allocate() for _ in lengths]
         for h, n in zip(hs, lengths):
@@ -155,3 +156,26 @@ def test_packed_metadata_out_of_range_is_flagged():
     torch.cuda.synchronize()
     assert "packed batch metadata (q_start / q_len / request id) out of range" in ops.read_device_errors(ma.error_word)
     ma.error_word.zero_()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=str)
+def test_packed_step_with_prefill_schedule(dtype):
+    """The packed batch's prefill launch on a plan (its prefill requests, in prefill_ids
+    order) gives the default grid's rows within 2e-2 and the oracle's."""
+    lengths, query_lens = [0, 5, 9000, 130, 4095, 17, 2560], [1, 37, 300, 300, 1, 128, 600]
+    (ma, ha), (mb, hb) = twin_managers(lengths, query_lens, dtype, seed=11)
+    ma.prefill_plan = True
+    q, k, v = packed_inputs(query_lens, dtype, seed=4)
+    batch = ma.begin_batch(ha, query_lens)
+    planned = batch._prefill_schedule(q)
+    assert planned is not None  # this mix of chunks is scheduled
+    batch.write_layer(0, k, v)
+    out = batch.attend_layer(q, 0)
+    ref_batch = mb.begin_batch(hb, query_lens)
+    ref_batch.write_layer(0, k, v)
+    ref = ref_batch.attend_layer(q, 0)
+    torch.cuda.synchronize()
+    ma.check_device_errors()
+    assert (out.float() - ref.float()).abs().max().item() <= 2e-2
+    err = np.abs(out.float().cpu().numpy() - oracle_rows(ma, ha, query_lens, q)).max()
+    assert err <= TOL[dtype], err
