@@ -947,8 +947,9 @@ def main():
             # config 3 beside the headline (short: 50 timed steps)
             result["prefill"] = run_prefill(args, world, rank, local, peaks, peak_kind, steps=50, warmup=5,
                                             prefix_max=4096)
-            # the config-3 launch is short (~0.2 ms); the same shape on longer prefixes shows
-            # the kernel's steady state
+            # the config-3 launch is short (~0.2 ms, 3.5 CTA waves); the same shape on longer
+            # prefixes shows the kernel on long items (there the planned schedule cuts the
+            # heaviest in two)
             result["prefill_long_prefix"] = run_prefill(args, world, rank, local, peaks, peak_kind,
                                                         steps=20, warmup=3, prefix_max=32768)
     elif args.workload == "prefill":
