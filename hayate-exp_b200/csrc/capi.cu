@@ -462,7 +462,7 @@ int launch_generic(const void* q, const int64_t* qs, const void* k_pool, const v
 // half). The two constants are fitted to B200 timings of the default grid, longest-first
 // orders and split plans on four prefix sets (config 3, two random U[0, 4096] sets and
 // U[0, 32768]); a plan is used only when the model predicts it at least kMinGain faster.
-constexpr double kItemOverhead = 5.0, kMergeCost = 8.0, kMinGain = 0.03;
+constexpr double kItemOverhead = 5.0, kMergeCost = 8.0, kMinGain = 0.03;  // defaults
 
 struct PlanEntry {
   int32_t z, q_tile, pair, k_lo, k_hi, split;  // split: slot * 2 + part, or -1
@@ -487,7 +487,7 @@ double greedy_makespan(const std::vector<double>& costs, int sms) {
 // Items of the default grid, in its launch order (request, head pair, query tile from the
 // last), with their key-tile counts; false when a count does not fit the item encoding.
 bool prefill_items(const int32_t* cache_lens, const int32_t* q_lens, int32_t batch,
-                   int32_t query_len, int32_t pairs, std::vector<PlanEntry>* items) {
+                   int32_t query_len, int32_t pairs, double overhead, std::vector<PlanEntry>* items) {
   for (int32_t z = 0; z < batch; ++z) {
     const int64_t ql = q_lens != nullptr ? q_lens[z] : query_len;
     if (ql <= 0 || cache_lens[z] < 0) continue;
@@ -497,7 +497,7 @@ bool prefill_items(const int32_t* cache_lens, const int32_t* q_lens, int32_t bat
         const int64_t t_last = std::min<int64_t>(int64_t(qt) * 128 + 127, ql - 1);
         const int64_t n = (int64_t(cache_lens[z]) + t_last) / 128 + 1;
         if (n > 0xFFFF || qt > 0xFFFF || pair > 0xFFFF) return false;
-        items->push_back({z, qt, pair, 0, int32_t(n), -1, double(n) + kItemOverhead});
+        items->push_back({z, qt, pair, 0, int32_t(n), -1, double(n) + overhead});
       }
   }
   return true;
@@ -1068,8 +1068,8 @@ int hyt_paged_attention_packed_planned(
 
 int32_t hyt_prefill_plan(const int32_t* cache_lens, const int32_t* q_lens, int32_t batch,
                          int32_t query_len, int32_t num_q_heads, int32_t num_sms,
-                         int32_t max_splits, int32_t* items, int32_t max_items,
-                         int32_t* num_splits) {
+                         int32_t max_splits, float item_overhead, float merge_cost,
+                         int32_t* items, int32_t max_items, int32_t* num_splits) {
   g_last_error.clear();
   if (cache_lens == nullptr || items == nullptr || num_splits == nullptr)
     return fail(HYT_ERR_INVALID, "null pointer argument");
@@ -1077,8 +1077,10 @@ int32_t hyt_prefill_plan(const int32_t* cache_lens, const int32_t* q_lens, int32
       (q_lens == nullptr && query_len < 1))
     return fail(HYT_ERR_INVALID, "bad plan sizes");
   *num_splits = 0;
+  const double ov = item_overhead > 0.f ? item_overhead : kItemOverhead;
+  const double mc = merge_cost > 0.f ? merge_cost : kMergeCost;
   std::vector<PlanEntry> base;
-  if (!prefill_items(cache_lens, q_lens, batch, query_len, num_q_heads / 2, &base)) return 0;
+  if (!prefill_items(cache_lens, q_lens, batch, query_len, num_q_heads / 2, ov, &base)) return 0;
   if (base.empty()) return 0;
   std::vector<double> costs;
   for (const PlanEntry& e : base) costs.push_back(e.cost);
@@ -1097,7 +1099,7 @@ int32_t hyt_prefill_plan(const int32_t* cache_lens, const int32_t* q_lens, int32
     for (const PlanEntry& e : lpt) {
       if (slot < k && e.k_hi >= 2) {
         const int32_t mid = e.k_hi / 2;
-        const double c0 = mid + kItemOverhead + kMergeCost, c1 = (e.k_hi - mid) + kItemOverhead + kMergeCost;
+        const double c0 = mid + ov + mc, c1 = (e.k_hi - mid) + ov + mc;
         out->push_back({e.z, e.q_tile, e.pair, 0, mid, slot * 2, c0});
         out->push_back({e.z, e.q_tile, e.pair, mid, e.k_hi, slot * 2 + 1, c1});
         ++slot;

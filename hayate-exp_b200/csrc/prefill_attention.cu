@@ -48,9 +48,10 @@
 // Planned launches (PrefillPlan, made on the host by hyt_prefill_plan): a 1-D grid whose
 // CTA i takes item i of the plan (request, query tile, head pair, key-tile range), so
 // that the longest items start first. An item cut in two runs as two CTAs over the two
-// halves of its key tiles; each writes its partial (unnormalised O, running max, sum)
-// to its slot of the split workspace and the second to arrive merges both (the same
-// online-softmax merge as across tiles) and resets the slot's counter.
+// halves of its key tiles: the first to finish writes its partial (unnormalised O,
+// running max, sum) to its slot of the split workspace and publishes it; the second
+// merges it with its own O from TMEM (the same online-softmax merge as across tiles),
+// writes the rows and resets the slot's counter.
 //
 // FLOPs per launch counted by the roofline: 4 * H_q * 128 per causal-valid
 // (query, key) pair.
@@ -182,6 +183,22 @@ __device__ __forceinline__ void merge_split(const PrefillPlan& plan, int slot, c
   }
 }
 
+// Split slot counter: each half adds 1 when it arrives (bits 0-1 count arrivals) and the
+// first to arrive adds kPublished once its partial is in the workspace. The second half
+// (its add returned an arrival count of 1) waits, bounded by the pipeline-wait limit, for
+// that bit, then merges and zeroes the counter.
+constexpr int kPublished = 4;
+__device__ __forceinline__ void wait_published(int* counter, int prev, int32_t* error_word) {
+  if (prev & kPublished) return;
+  const uint64_t start = global_ns();
+  while (!(*reinterpret_cast<volatile int*>(counter) & kPublished)) {
+    if (global_ns() - start > kWaitLimitNs) {
+      flag_error(error_word, HYT_DEVERR_WAIT_TIMEOUT);
+      return;
+    }
+  }
+}
+
 // 96 registers: 18 warps over 4 sub-partitions put 5 warps on one 16K-register file.
 template <typename T, bool kPacked>
 __global__ void __maxnreg__(96)
@@ -234,16 +251,22 @@ __global__ void __maxnreg__(96)
   auto empty_split = [&](bool rows_known, int query_len) {
     if (split < 0) return;
     const int slot = split >> 1, part = split & 1;
+    int* counter = P.plan.ws_counter + slot;
     float2* ml = reinterpret_cast<float2*>(P.plan.ws_ml) + (int64_t(slot) * 2 + part) * 2 * kRows;
     for (int i = threadIdx.x; i < 2 * kRows; i += kThreads) ml[i] = make_float2(-INFINITY, 0.f);
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) bars->last = atomicAdd(&P.plan.ws_counter[slot], 1) == 1;
+    if (threadIdx.x == 0) bars->last = atomicAdd(counter, 1);
     __syncthreads();
-    if (bars->last) {
+    const int prev = *reinterpret_cast<volatile int32_t*>(&bars->last);
+    if ((prev & 3) == 0) {  // first: the empty partial is published
+      if (threadIdx.x == 0) atomicAdd(counter, kPublished);
+    } else {  // second: merge the partner's partial with the empty one
+      if (threadIdx.x == 0) wait_published(counter, prev, p.error_word);
+      __syncthreads();
       __threadfence();
       if (rows_known) merge_split<T>(P.plan, slot, p, h0, t0, query_len, o_row, threadIdx.x, kThreads);
-      if (threadIdx.x == 0) P.plan.ws_counter[slot] = 0;
+      if (threadIdx.x == 0) *counter = 0;
     }
   };
   if (!item_ok) {
@@ -601,51 +624,85 @@ __global__ void __maxnreg__(96)
     const float l = red_sum[r] + red_sum[kRows + r];
     // a refused page table: zeros (`bad` is published by the producer's prod_done arrival)
     const bool refused = *reinterpret_cast<volatile int32_t*>(&bars->bad) != 0;
+    // split item: the half that arrives first writes its partial (unnormalised O, running
+    // max, sum; consecutive lanes -> consecutive rows of a 16-byte column chunk) and
+    // publishes it; the second merges it with its own O (still in TMEM) and writes the
+    // rows. A refused half contributes nothing (sum 0).
+    float own_scale = 1.f, partner_scale = 0.f, inv = l > 0.f ? 1.f / l : 0.f;
+    bool use_own = !refused;
+    const float4* partner = nullptr;
+    bool write_rows = true;
     if (split >= 0) {
-      // one half of a split item: its partial (O, running max, sum) goes to the workspace
-      // (consecutive lanes -> consecutive rows of a 16-byte column chunk); the half that
-      // arrives second merges both and resets the slot's counter. A refused half adds 0.
       const int slot = split >> 1, part = split & 1;
-      const int64_t unit = (int64_t(slot) * 2 + part) * 2 + x;
-      float4* wo = reinterpret_cast<float4*>(P.plan.ws_o) + unit * 32 * kRows;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t o[32];
-        tmem_ld32(lane_addr + o_col + c * 32, o);
-        tmem_wait_ld();
-#pragma unroll
-        for (int v = 0; v < 8; ++v)
-          wo[(half * 16 + c * 8 + v) * kRows + r] =
-              make_float4(__uint_as_float(o[4 * v]), __uint_as_float(o[4 * v + 1]),
-                          __uint_as_float(o[4 * v + 2]), __uint_as_float(o[4 * v + 3]));
-      }
-      if (half == 0)
-        reinterpret_cast<float2*>(P.plan.ws_ml)[unit * kRows + r] = make_float2(m_run, refused ? 0.f : l);
-      __threadfence();
+      int* counter = P.plan.ws_counter + slot;
+      if (threadIdx.x == 0) bars->last = atomicAdd(counter, 1);
       named_bar_sync(kSoftmaxBar, kSoftmaxThreads);
-      if (threadIdx.x == 0) bars->last = atomicAdd(&P.plan.ws_counter[slot], 1) == 1;
-      named_bar_sync(kSoftmaxBar, kSoftmaxThreads);
-      if (*reinterpret_cast<volatile int32_t*>(&bars->last)) {
+      const int prev = *reinterpret_cast<volatile int32_t*>(&bars->last);
+      if ((prev & 3) == 0) {  // first
+        const int64_t unit = (int64_t(slot) * 2 + part) * 2 + x;
+        float4* wo = reinterpret_cast<float4*>(P.plan.ws_o) + unit * 32 * kRows;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t o[32];
+          tmem_ld32(lane_addr + o_col + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            wo[(half * 16 + c * 8 + v) * kRows + r] =
+                make_float4(__uint_as_float(o[4 * v]), __uint_as_float(o[4 * v + 1]),
+                            __uint_as_float(o[4 * v + 2]), __uint_as_float(o[4 * v + 3]));
+        }
+        if (half == 0)
+          reinterpret_cast<float2*>(P.plan.ws_ml)[unit * kRows + r] = make_float2(m_run, refused ? 0.f : l);
         __threadfence();
-        merge_split<T>(P.plan, slot, p, h0, t0, query_len, o_row, threadIdx.x, kSoftmaxThreads);
-        if (threadIdx.x == 0) P.plan.ws_counter[slot] = 0;
+        named_bar_sync(kSoftmaxBar, kSoftmaxThreads);
+        if (threadIdx.x == 0) atomicAdd(counter, kPublished);
+        write_rows = false;
+      } else {  // second
+        if (threadIdx.x == 0) wait_published(counter, prev, err);
+        named_bar_sync(kSoftmaxBar, kSoftmaxThreads);
+        __threadfence();
+        const int64_t unit = (int64_t(slot) * 2 + (part ^ 1)) * 2 + x;
+        const float2 other = __ldcg(reinterpret_cast<const float2*>(P.plan.ws_ml) + unit * kRows + r);
+        const float own_l = refused ? 0.f : l;
+        const bool use_other = other.y > 0.f;
+        use_own = own_l > 0.f;
+        const float m = use_own && use_other ? fmaxf(m_run, other.x) : (use_own ? m_run : (use_other ? other.x : 0.f));
+        own_scale = use_own ? ex2(m_run - m) : 0.f;
+        partner_scale = use_other ? ex2(other.x - m) : 0.f;
+        const float lsum = own_l * own_scale + other.y * partner_scale;
+        inv = lsum > 0.f ? 1.f / lsum : 0.f;
+        if (use_other) partner = reinterpret_cast<const float4*>(P.plan.ws_o) + unit * 32 * kRows;
+        if (threadIdx.x == 0) *counter = 0;  // both halves are done with the slot
       }
-    } else {
-    const float inv = l > 0.f ? 1.f / l : 0.f;
+    }
+    if (write_rows) {
     uint8_t* stage = smem + kKOff + x * kRows * kStageRowBytes + half * 128;
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       uint32_t o[32];
       tmem_ld32(lane_addr + o_col + c * 32, o);
       tmem_wait_ld();
+      float f[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) f[i] = use_own ? __uint_as_float(o[i]) * own_scale : 0.f;
+      if (partner != nullptr) {
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          const float4 q4 = __ldcg(&partner[(half * 16 + c * 8 + v) * kRows + r]);
+          f[4 * v] += q4.x * partner_scale;
+          f[4 * v + 1] += q4.y * partner_scale;
+          f[4 * v + 2] += q4.z * partner_scale;
+          f[4 * v + 3] += q4.w * partner_scale;
+        }
+      }
 #pragma unroll
       for (int v = 0; v < 4; ++v) {
         uint4 w;
-        w.x = Elem<T>::pack2(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
-        w.y = Elem<T>::pack2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
-        w.z = Elem<T>::pack2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
-        w.w = Elem<T>::pack2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
-        if (refused) w = make_uint4(0u, 0u, 0u, 0u);
+        w.x = Elem<T>::pack2(f[8 * v + 0] * inv, f[8 * v + 1] * inv);
+        w.y = Elem<T>::pack2(f[8 * v + 2] * inv, f[8 * v + 3] * inv);
+        w.z = Elem<T>::pack2(f[8 * v + 4] * inv, f[8 * v + 5] * inv);
+        w.w = Elem<T>::pack2(f[8 * v + 6] * inv, f[8 * v + 7] * inv);
         *reinterpret_cast<uint4*>(stage + r * kStageRowBytes + (c * 4 + v) * 16) = w;
       }
     }

@@ -64,7 +64,8 @@ SIGNATURES = {
                                                   _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_f32, _c_p,
                                                   _c_i32, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_p,
                                                   _c_size, _c_p, _c_p]),
-    "hyt_prefill_plan": (_c_i32, [_c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_i32, _c_p]),
+    "hyt_prefill_plan": (_c_i32, [_c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_f32, _c_f32,
+                                  _c_p, _c_i32, _c_p]),
     "hyt_prefill_workspace_bytes": (_c_size, [_c_i32]),
     "hyt_prefill_attention_planned": (ctypes.c_int, _ATTENTION_ARGS + [_c_p, _c_i32, _c_i32, _c_p, _c_size,
                                                                        _c_p, _c_p]),

@@ -408,11 +408,12 @@ def wait_self_test(error_word: torch.Tensor) -> tuple[int, int]:
 
 # ---------------------------------------------------------------------------- prefill schedule
 def prefill_plan(cache_lens, query_len: int, num_q_heads: int, num_sms: int, max_splits: int = 128,
-                 q_lens=None):
+                 q_lens=None, item_overhead: float = 0.0, merge_cost: float = 0.0):
     """Host-side schedule for the prefill kernel (``hyt_prefill_plan``).
 
-    ``cache_lens`` / ``q_lens`` are host sequences (one entry per request of the launch).
-    Returns ``(items, num_splits)``: ``items`` an int32 ``[n, 4]`` array for
+    ``cache_lens`` / ``q_lens`` are host sequences (one entry per request of the launch);
+    ``item_overhead`` / ``merge_cost`` override the cost model's constants (key tiles;
+    0 keeps the library's defaults). Returns ``(items, num_splits)``: ``items`` an int32 ``[n, 4]`` array for
     ``prefill_attention_planned``, or ``None`` when the default grid is at least as good.
     """
     import numpy as np
@@ -426,8 +427,8 @@ def prefill_plan(cache_lens, query_len: int, num_q_heads: int, num_sms: int, max
     items = np.zeros((max(max_items, 1), 4), dtype=np.int32)
     splits = ctypes.c_int32(0)
     n = _lib.lib().hyt_prefill_plan(lens.ctypes.data, None if ql is None else ql.ctypes.data, batch,
-                                    qmax, num_q_heads, num_sms, max_splits, items.ctypes.data,
-                                    max_items, ctypes.byref(splits))
+                                    qmax, num_q_heads, num_sms, max_splits, item_overhead, merge_cost,
+                                    items.ctypes.data, max_items, ctypes.byref(splits))
     if n < 0:
         _lib.check(n, "hyt_prefill_plan")
     return (items[:n].copy(), int(splits.value)) if n > 0 else (None, 0)

@@ -265,15 +265,17 @@ int hyt_paged_attention_packed(const void* q, const int64_t* q_strides, const vo
  * grid is fixed); a planned launch computes the same rows as hyt_prefill_attention.
  * cache_lens / q_lens are HOST arrays (q_lens NULL: every request has query_len queries).
  * The plan is chosen by simulating the block scheduler on num_sms SMs for the default
- * grid and for longest-first orders with 0..max_splits items cut; items (4 int32 each,
+ * grid and for longest-first orders with 0..max_splits items cut, in a cost model
+ * counted in key tiles: an item costs its tiles + item_overhead, a half of a cut item
+ * also pays merge_cost (<= 0: the defaults fitted on a B200); items (4 int32 each,
  * room for max_items) receives it. Returns the number of items, 0 when the default grid
  * is at least as good (launch without a plan), negative on bad arguments.
  * *num_splits receives the number of split slots the plan uses.
  */
 int32_t hyt_prefill_plan(const int32_t* cache_lens, const int32_t* q_lens, int32_t batch,
                          int32_t query_len, int32_t num_q_heads, int32_t num_sms,
-                         int32_t max_splits, int32_t* items, int32_t max_items,
-                         int32_t* num_splits);
+                         int32_t max_splits, float item_overhead, float merge_cost,
+                         int32_t* items, int32_t max_items, int32_t* num_splits);
 
 /* Workspace bytes a plan with num_splits split slots needs (its counters must be zero
  * before first use, hyt_workspace_init; the kernel leaves them zero). */
