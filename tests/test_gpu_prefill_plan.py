@@ -120,3 +120,27 @@ def test_planned_prefill_refused_page_then_clean_call():
     m.check_device_errors()
     err2 = np.abs(out.float().cpu().numpy()[[1]] - oracle_rows(m, batch, q, [1])[[1]]).max()
     assert err2 <= 2e-2, err2
+
+
+def test_planned_prefill_refused_request_both_halves_exit_early():
+    """A request refused before any load (negative cache length): both halves of its cut
+    items take the early path with empty partials; its rows are zeros, the counters end
+    at zero and the next call is clean."""
+    lengths, query_len = SPLIT
+    m, hs, batch, q = build(lengths, query_len, seed=6)
+    items, splits = batch._prefill_schedule(q)
+    lens = batch.cache_lens_i32.clone()
+    lens[1] = -1
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ws = m.prefill_workspace(splits)
+    out = ops.prefill_attention_planned(q, m.k_cache, m.v_cache, 0, batch.page_table, lens, 128, items,
+                                        splits, workspace=ws, error_word=err)
+    torch.cuda.synchronize()
+    assert "kv length needs more pages than the page table row holds" in ops.read_device_errors(err)
+    assert float(out[1].float().abs().max()) == 0.0
+    assert int(ws[: 4 * splits].view(torch.int32).abs().sum().item()) == 0
+    good = batch.attend_layer(q, 0)
+    torch.cuda.synchronize()
+    m.check_device_errors()
+    err2 = np.abs(good.float().cpu().numpy()[[1]] - oracle_rows(m, batch, q, [1])[[1]]).max()
+    assert err2 <= 2e-2, err2
