@@ -116,6 +116,17 @@ def check(rc: int, what: str) -> None:
         raise RuntimeError(f"{what} failed ({rc}): {message}")
 
 
+_int64_arrays: dict = {}
+
+
 def int64_array(values) -> ctypes.Array:
-    values = list(values)
-    return (ctypes.c_int64 * len(values))(*values)
+    """A ctypes int64 array of ``values`` (the C side only reads it: equal tuples share one,
+    so per-call stride arrays cost a dictionary lookup)."""
+    key = tuple(int(v) for v in values)
+    arr = _int64_arrays.get(key)
+    if arr is None:
+        if len(_int64_arrays) > 4096:
+            _int64_arrays.clear()
+        arr = (ctypes.c_int64 * len(key))(*key)
+        _int64_arrays[key] = arr
+    return arr

@@ -8,6 +8,7 @@ message if the call is refused. All launches go on the current CUDA stream.
 from __future__ import annotations
 
 import ctypes
+import functools
 import math
 
 import torch
@@ -135,9 +136,12 @@ def norm_rope_scatter(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_norm_
     return q_out
 
 
+@functools.lru_cache(maxsize=1024)
 def attention_workspace_bytes(batch: int, query_len: int, num_q_heads: int, num_kv_heads: int,
                               head_dim: int, max_kv_len: int, dtype: torch.dtype,
                               split_tokens: int = 0) -> int:
+    """Workspace bytes of a decode launch (``hyt_attention_workspace_bytes``; a pure function
+    of its arguments, cached: every layer of every step asks)."""
     return int(_lib.lib().hyt_attention_workspace_bytes(batch, query_len, num_q_heads, num_kv_heads,
                                                         head_dim, max_kv_len, split_tokens,
                                                         dtype_code(dtype)))
