@@ -463,6 +463,7 @@ int launch_generic(const void* q, const int64_t* qs, const void* k_pool, const v
 // orders and split plans on four prefix sets (config 3, two random U[0, 4096] sets and
 // U[0, 32768]); a plan is used only when the model predicts it at least kMinGain faster.
 constexpr double kItemOverhead = 5.0, kMergeCost = 8.0, kMinGain = 0.03;  // defaults
+constexpr int kMaxPlannedItemsPerSm = 24;  // beyond this many items per SM: the default grid
 
 struct PlanEntry {
   int32_t z, q_tile, pair, k_lo, k_hi, split;  // split: slot * 2 + part, or -1
@@ -1081,7 +1082,9 @@ int32_t hyt_prefill_plan(const int32_t* cache_lens, const int32_t* q_lens, int32
   const double mc = merge_cost > 0.f ? merge_cost : kMergeCost;
   std::vector<PlanEntry> base;
   if (!prefill_items(cache_lens, q_lens, batch, query_len, num_q_heads / 2, ov, &base)) return 0;
-  if (base.empty()) return 0;
+  // with many waves the last one is a small share of the launch: not worth the host time
+  // (about 1 ms per 500 items)
+  if (base.empty() || base.size() > size_t(kMaxPlannedItemsPerSm) * size_t(num_sms)) return 0;
   std::vector<double> costs;
   for (const PlanEntry& e : base) costs.push_back(e.cost);
   const double grid = greedy_makespan(costs, num_sms);  // the default grid
