@@ -205,3 +205,62 @@ def test_packed_scatter_rejects_bad_arguments():
     args[14] = 0  # total_tokens
     assert lib.hyt_kv_scatter_packed(*args) == -1
     assert "total_tokens" in lib.hyt_last_error().decode()
+
+
+def _planned_args(**overrides):
+    """hyt_prefill_attention_planned arguments for a shape the prefill kernel takes (16-byte
+    aligned fake pointers: nothing is dereferenced before the checks return)."""
+    s = _lib.int64_array([0, 0, 0])
+    args = dict(q=16, qs=s, k_pool=16, v_pool=16, num_layers=1, layer=0, capacity=4096,
+                page_table=16, pts=32, cache_lens=16, out=16, os=s, batch=2, query_len=256,
+                hq=32, hkv=8, head_dim=128, page_size=128, dtype=0, scale=0.088,
+                items=16, num_items=4, num_splits=0, ws=None, ws_bytes=0, err=None, stream=None)
+    args.update(overrides)
+    return list(args.values())
+
+
+@pytest.mark.parametrize("bad, code, message", [
+    (dict(q=None), -1, "null pointer"),
+    (dict(num_items=-1), -1, "bad plan"),
+    (dict(items=None), -1, "bad plan"),
+    (dict(num_splits=2), -4, "hyt_prefill_workspace_bytes"),
+    (dict(num_splits=2, ws=16, ws_bytes=1024), -4, "hyt_prefill_workspace_bytes"),
+    (dict(head_dim=64), -2, "prefill kernel needs"),
+])
+def test_planned_prefill_rejects_bad_arguments(bad, code, message):
+    lib = _lib.lib()
+    rc = lib.hyt_prefill_attention_planned(*_planned_args(**bad))
+    assert rc == code
+    assert message in lib.hyt_last_error().decode()
+
+
+def test_planned_packed_attention_rejects_bad_plans():
+    lib = _lib.lib()
+    base = _packed_args()
+    head, tail = base[:-2], base[-2:]  # ... workspace_bytes | error_word, stream
+    assert lib.hyt_paged_attention_packed_planned(*head, None, 3, 0, None, 0, *tail) == -1
+    assert "bad plan" in lib.hyt_last_error().decode()
+    assert lib.hyt_paged_attention_packed_planned(*head, 16, 3, 4, None, 0, *tail) == -4
+    assert "hyt_prefill_workspace_bytes" in lib.hyt_last_error().decode()
+
+
+def test_fused_scatter_entry_rejects_null_rows():
+    lib = _lib.lib()
+    a = _attention_args()
+    s6 = _lib.int64_array([0] * 6)
+    # q, qs | k_new, v_new, new_strides | k_pool ... (the hyt_paged_attention arguments)
+    rc = lib.hyt_paged_attention_scatter(a[0], a[1], None, 1, s6, *a[2:])
+    assert rc == -1
+    assert "null pointer" in lib.hyt_last_error().decode()
+
+
+def test_prefill_plan_and_self_test_reject_bad_arguments():
+    lib = _lib.lib()
+    n = ctypes.c_int32(0)
+    items = (ctypes.c_int32 * 16)()
+    lens = (ctypes.c_int32 * 2)(10, 20)
+    assert lib.hyt_prefill_plan(None, None, 2, 64, 32, 148, 8, 0.0, 0.0, items, 4, ctypes.byref(n)) == -1
+    assert lib.hyt_prefill_plan(lens, None, 0, 64, 32, 148, 8, 0.0, 0.0, items, 4, ctypes.byref(n)) == -1
+    assert lib.hyt_prefill_plan(lens, None, 2, 64, 32, 0, 8, 0.0, 0.0, items, 4, ctypes.byref(n)) == -1
+    assert lib.hyt_wait_self_test(None, None, None) == -1
+    assert "null" in lib.hyt_last_error().decode()
