@@ -504,6 +504,27 @@ bool prefill_items(const int32_t* cache_lens, const int32_t* q_lens, int32_t bat
   return true;
 }
 
+// Split workspace of a plan: [counters (int32 per slot, 256-byte padded) | (max, sum) per
+// slot, half, head and row | partial O per slot, half, head, 16-byte column chunk and row].
+size_t split_counter_bytes(int32_t num_splits) { return (size_t(num_splits) * 4 + 255) / 256 * 256; }
+
+hyt::PrefillPlan make_prefill_plan(const int32_t* items, int32_t num_items, int32_t num_splits,
+                                   void* workspace) {
+  hyt::PrefillPlan plan{nullptr, 0, 0, nullptr, nullptr, nullptr};
+  if (num_items <= 0) return plan;
+  plan.items = reinterpret_cast<const hyt::PrefillItem*>(items);
+  plan.num_items = num_items;
+  plan.num_splits = num_splits;
+  if (num_splits > 0) {
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const size_t cb = split_counter_bytes(num_splits), ml_bytes = size_t(num_splits) * 2 * 2 * 128 * 2 * 4;
+    plan.ws_counter = reinterpret_cast<int32_t*>(ws);
+    plan.ws_ml = reinterpret_cast<float*>(ws + cb);
+    plan.ws_o = reinterpret_cast<float*>(ws + cb + ml_bytes);
+  }
+  return plan;
+}
+
 // ------------------------------------------------------------------ static decode scratch
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
@@ -1028,8 +1049,6 @@ int hyt_paged_attention_packed(const void* q, const int64_t* q_strides, const vo
                           workspace_bytes, error_word, stream, nullptr);
 }
 
-static size_t prefill_counter_bytes(int32_t num_splits);
-
 int hyt_paged_attention_packed_planned(
     const void* q, const int64_t* q_strides, const void* k_pool, const void* v_pool,
     int32_t num_layers, int32_t layer, int64_t capacity_tokens, const int32_t* page_table,
@@ -1047,18 +1066,7 @@ int hyt_paged_attention_packed_planned(
   if (num_items > 0 && num_splits > 0 &&
       (plan_workspace == nullptr || plan_workspace_bytes < hyt_prefill_workspace_bytes(num_splits)))
     return fail(HYT_ERR_WORKSPACE, "plan workspace missing or smaller than hyt_prefill_workspace_bytes()");
-  hyt::PrefillPlan plan{nullptr, 0, 0, nullptr, nullptr, nullptr};
-  if (num_items > 0) {
-    uint8_t* ws = static_cast<uint8_t*>(plan_workspace);
-    const size_t cb = num_splits > 0 ? prefill_counter_bytes(num_splits) : 0;
-    const size_t ml_bytes = size_t(num_splits) * 2 * 2 * 128 * 2 * 4;
-    plan.items = reinterpret_cast<const hyt::PrefillItem*>(items);
-    plan.num_items = num_items;
-    plan.num_splits = num_splits;
-    plan.ws_counter = num_splits > 0 ? reinterpret_cast<int32_t*>(ws) : nullptr;
-    plan.ws_ml = num_splits > 0 ? reinterpret_cast<float*>(ws + cb) : nullptr;
-    plan.ws_o = num_splits > 0 ? reinterpret_cast<float*>(ws + cb + ml_bytes) : nullptr;
-  }
+  const hyt::PrefillPlan plan = make_prefill_plan(items, num_items, num_splits, plan_workspace);
   return packed_attention(q, q_strides, k_pool, v_pool, num_layers, layer, capacity_tokens,
                           page_table, page_table_stride, cache_lens, q_start, q_len, out,
                           out_strides, batch, total_tokens, num_q_heads, num_kv_heads, head_dim,
@@ -1140,12 +1148,9 @@ int32_t hyt_prefill_plan(const int32_t* cache_lens, const int32_t* q_lens, int32
   return int32_t(cand.size());
 }
 
-// Split workspace: [counters (int32 per slot, 256-byte padded) | (max, sum) | partial O].
-static size_t prefill_counter_bytes(int32_t num_splits) { return (size_t(num_splits) * 4 + 255) / 256 * 256; }
-
 size_t hyt_prefill_workspace_bytes(int32_t num_splits) {
   if (num_splits <= 0) return 0;
-  return prefill_counter_bytes(num_splits) + size_t(num_splits) * size_t(hyt::kPrefillSplitSlotBytes);
+  return split_counter_bytes(num_splits) + size_t(num_splits) * size_t(hyt::kPrefillSplitSlotBytes);
 }
 
 int hyt_prefill_attention_planned(const void* q, const int64_t* q_strides, const void* k_pool,
@@ -1177,15 +1182,7 @@ int hyt_prefill_attention_planned(const void* q, const int64_t* q_strides, const
   if (num_items == 0)  // no plan: the default grid
     return launch_prefill(q, q_strides, k_pool, v_pool, g, page_table, cache_lens, out,
                           out_strides, scale, error_word, static_cast<cudaStream_t>(stream));
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  hyt::PrefillPlan plan;
-  plan.items = reinterpret_cast<const hyt::PrefillItem*>(items);
-  plan.num_items = num_items;
-  plan.num_splits = num_splits;
-  const size_t cb = prefill_counter_bytes(num_splits), ml_bytes = size_t(num_splits) * 2 * 2 * 128 * 2 * 4;
-  plan.ws_counter = num_splits > 0 ? reinterpret_cast<int32_t*>(ws) : nullptr;
-  plan.ws_ml = num_splits > 0 ? reinterpret_cast<float*>(ws + cb) : nullptr;
-  plan.ws_o = num_splits > 0 ? reinterpret_cast<float*>(ws + cb + ml_bytes) : nullptr;
+  const hyt::PrefillPlan plan = make_prefill_plan(items, num_items, num_splits, workspace);
   return launch_prefill(q, q_strides, k_pool, v_pool, g, page_table, cache_lens, out,
                         out_strides, scale, error_word, static_cast<cudaStream_t>(stream), nullptr,
                         &plan);

@@ -372,13 +372,7 @@ def paged_attention_packed(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.
         rc = _lib.lib().hyt_paged_attention_packed(*common, _ptr(error_word), _stream_ptr())
         _lib.check(rc, "hyt_paged_attention_packed")
         return out
-    _require_cuda(plan_items)
-    if plan_items.dtype != torch.int32 or plan_items.dim() != 2 or plan_items.shape[1] != 4 \
-            or not plan_items.is_contiguous():
-        raise ValueError("plan_items must be a contiguous int32 [n, 4] CUDA tensor")
-    pneed = prefill_workspace_bytes(plan_splits)
-    if pneed and (plan_workspace is None or plan_workspace.numel() < pneed):
-        raise RuntimeError(f"the plan needs a zeroed workspace of {pneed} bytes")
+    pneed = _check_plan(plan_items, plan_splits, plan_workspace)
     rc = _lib.lib().hyt_paged_attention_packed_planned(
         *common, plan_items.data_ptr(), plan_items.shape[0], plan_splits,
         _ptr(plan_workspace) if pneed else None, plan_workspace.numel() if pneed else 0,
@@ -442,6 +436,17 @@ def prefill_workspace_bytes(num_splits: int) -> int:
     return int(_lib.lib().hyt_prefill_workspace_bytes(num_splits))
 
 
+def _check_plan(items: torch.Tensor, num_splits: int, workspace: torch.Tensor | None) -> int:
+    """Validate a plan's device items and split workspace; returns the workspace bytes needed."""
+    _require_cuda(items)
+    if items.dtype != torch.int32 or items.dim() != 2 or items.shape[1] != 4 or not items.is_contiguous():
+        raise ValueError("plan items must be a contiguous int32 [n, 4] CUDA tensor")
+    need = prefill_workspace_bytes(num_splits)
+    if need and (workspace is None or workspace.numel() < need):
+        raise RuntimeError(f"the plan needs a zeroed workspace of {need} bytes")
+    return need
+
+
 def prefill_attention_planned(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, layer: int,
                               page_table: torch.Tensor, cache_lens: torch.Tensor, page_size: int,
                               items: torch.Tensor | None, num_splits: int,
@@ -460,15 +465,8 @@ def prefill_attention_planned(q: torch.Tensor, k_pool: torch.Tensor, v_pool: tor
                           device=q.device).transpose(1, 2)
     if out.shape != q.shape or out.dtype != q.dtype:
         raise ValueError("out must match q")
-    n_items = 0
-    if items is not None:
-        _require_cuda(items)
-        if items.dtype != torch.int32 or items.dim() != 2 or items.shape[1] != 4 or not items.is_contiguous():
-            raise ValueError("items must be a contiguous int32 [n, 4] CUDA tensor")
-        n_items = items.shape[0]
-    need = prefill_workspace_bytes(num_splits) if n_items else 0
-    if need and (workspace is None or workspace.numel() < need):
-        raise RuntimeError(f"the plan needs a zeroed workspace of {need} bytes")
+    n_items = 0 if items is None else items.shape[0]
+    need = _check_plan(items, num_splits, workspace) if n_items else 0
     qs = _lib.int64_array(_bht_strides(q, "q"))
     os_ = _lib.int64_array(_bht_strides(out, "out"))
     pts = _table_args(page_table, cache_lens, batch)
