@@ -566,7 +566,7 @@ def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=N
         barrier(world)
     manager.check_device_errors()
     out = step()  # the rows (compared with the reference's when --reference-gpu)
-    plan = batch._prefill_schedule(q)
+    plan = batch.prefill_schedule(q)
     schedule = ("default grid" if plan is None else
                 f"planned: {plan[0].shape[0]} CTAs, {plan[1]} items cut in two (longest first)")
     step_ms = sum(a.elapsed_time(c) for a, _, c in evs) / steps

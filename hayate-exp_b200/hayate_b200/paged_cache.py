@@ -256,7 +256,7 @@ class PagedKVBatch:
             workspace = self.workspace
             if workspace is None and n_dec:
                 workspace = manager.workspace_for(n_dec, 1, q.shape[1], self.max_kv_len)
-            planned = self._prefill_schedule(q)
+            planned = self.prefill_schedule(q)
             items, splits = planned if planned is not None else (None, 0)
             return ops.paged_attention_packed(
                 q, self.k_cache, self.v_cache, layer_idx, self.page_table, self.cache_lens_i32,
@@ -264,7 +264,7 @@ class PagedKVBatch:
                 self.query_len, self.max_kv_len, workspace=workspace, error_word=manager.error_word,
                 split_tokens=manager.split_tokens, plan_items=items, plan_splits=splits,
                 plan_workspace=manager.prefill_workspace(splits) if items is not None else None)
-        planned = self._prefill_schedule(q)
+        planned = self.prefill_schedule(q)
         if planned is not None:
             items, splits = planned
             return ops.prefill_attention_planned(
@@ -305,7 +305,7 @@ class PagedKVBatch:
                                            error_word=manager.error_word,
                                            split_tokens=manager.split_tokens)
 
-    def _prefill_schedule(self, q: torch.Tensor):
+    def prefill_schedule(self, q: torch.Tensor):
         """(items, splits) for a planned prefill launch of this batch, or None for the
         library's own dispatch. The plan (``ops.prefill_plan``: longest items first, the
         heaviest cut in two) is made on the host once per batch and head count and reused

@@ -167,7 +167,7 @@ def test_packed_step_with_prefill_schedule(dtype):
     ma.prefill_plan = True
     q, k, v = packed_inputs(query_lens, dtype, seed=4)
     batch = ma.begin_batch(ha, query_lens)
-    planned = batch._prefill_schedule(q)
+    planned = batch.prefill_schedule(q)
     assert planned is not None  # this mix of chunks is scheduled
     batch.write_layer(0, k, v)
     out = batch.attend_layer(q, 0)

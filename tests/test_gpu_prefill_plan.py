@@ -57,7 +57,7 @@ SPLIT = ([0, 9000], 300)
 @pytest.mark.parametrize("lengths, query_len", CASES, ids=str)
 def test_planned_prefill_matches_default_grid_and_oracle(lengths, query_len, dtype):
     m, hs, batch, q = build(lengths, query_len, dtype, seed=len(lengths) + query_len)
-    planned = batch._prefill_schedule(q)
+    planned = batch.prefill_schedule(q)
     out = batch.attend_layer(q, 0)
     m.prefill_plan = False
     ref = m.begin_batch(hs, query_len).attend_layer(q, 0)
@@ -87,13 +87,13 @@ def test_plan_choices():
 
 def batch_plan(lengths, query_len):
     m, hs, batch, q = build(lengths, query_len, seed=1)
-    return batch._prefill_schedule(q)
+    return batch.prefill_schedule(q)
 
 
 def test_split_plan_is_deterministic():
     lengths, query_len = SPLIT
     m, hs, batch, q = build(lengths, query_len, seed=3)
-    planned = batch._prefill_schedule(q)
+    planned = batch.prefill_schedule(q)
     assert planned is not None and planned[1] > 0  # this batch gets split items
     outs = [batch.attend_layer(q, 0) for _ in range(4)]  # one plan, several layers
     torch.cuda.synchronize()
@@ -104,7 +104,7 @@ def test_split_plan_is_deterministic():
 def test_planned_prefill_refused_page_then_clean_call():
     lengths, query_len = SPLIT
     m, hs, batch, q = build(lengths, query_len, seed=5)
-    items, splits = batch._prefill_schedule(q)
+    items, splits = batch.prefill_schedule(q)
     assert splits > 0
     table = batch.page_table.clone()
     table[1, 3] = m.num_pages + 1  # request 1 (prefix 9000): its items are the split ones
@@ -128,7 +128,7 @@ def test_planned_prefill_refused_request_both_halves_exit_early():
     at zero and the next call is clean."""
     lengths, query_len = SPLIT
     m, hs, batch, q = build(lengths, query_len, seed=6)
-    items, splits = batch._prefill_schedule(q)
+    items, splits = batch.prefill_schedule(q)
     lens = batch.cache_lens_i32.clone()
     lens[1] = -1
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
