@@ -85,3 +85,57 @@ def test_plan_rejects_bad_arguments():
         ops.prefill_plan([10, 20], 0, 32, 148, 8)  # no q_lens and query_len 0
     assert ops.prefill_workspace_bytes(0) == 0
     assert ops.prefill_workspace_bytes(3) >= 3 * 266240
+
+
+def model_choice(cache_lens, q_len, pairs, sms, max_splits, ov=5.0, mc=8.0, min_gain=0.03):
+    """The planner's decision restated: greedy makespans of the default grid and of
+    longest-first orders with the k heaviest items cut; returns the chosen k or None."""
+    import heapq
+
+    def makespan(costs):
+        free = [0.0] * sms
+        end = 0.0
+        for c in costs:
+            t = heapq.heappop(free) + c
+            heapq.heappush(free, t)
+            end = max(end, t)
+        return end
+
+    base = []
+    for z, cl in enumerate(cache_lens):
+        tiles = -(-q_len // 128)
+        for pair in range(pairs):
+            for qt in reversed(range(tiles)):
+                base.append(key_tiles(cl, q_len, qt))
+    grid = makespan([n + ov for n in base])
+    lpt = sorted(base, key=lambda n: -(n + ov))  # stable, like the C++ stable_sort
+    splittable = sum(n >= 2 for n in lpt)
+    best, best_k = grid, None
+    for k in (0, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256, 384, 512):
+        if k > min(max_splits, splittable):
+            break
+        costs, slot = [], 0
+        for n in lpt:
+            if slot < k and n >= 2:
+                costs += [n // 2 + ov + mc, (n - n // 2) + ov + mc]
+                slot += 1
+            else:
+                costs.append(n + ov)
+        m = makespan(sorted(costs, reverse=True))
+        if m < best - 1e-9:
+            best, best_k = m, k
+    if best_k is None or best > (1 - min_gain) * grid:
+        return None
+    return best_k
+
+
+@pytest.mark.parametrize("seed", range(8))
+def test_plan_choice_matches_the_model(seed):
+    rng = random.Random(100 + seed)
+    cache_lens = [rng.randint(0, rng.choice([4096, 16384, 32768])) for _ in range(rng.randint(1, 8))]
+    expect = model_choice(cache_lens, 512, 16, 148, 128)
+    items, splits = ops.prefill_plan(cache_lens, 512, 32, 148, 128)
+    if expect is None:
+        assert items is None
+    else:
+        assert items is not None and splits == expect
