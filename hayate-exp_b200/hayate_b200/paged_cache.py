@@ -420,7 +420,22 @@ class StaticDecodeBatch:
 
 
 class PagedKVCacheManager:
-    """Allocate fixed-size, reference-counted pages from shared K/V pools."""
+    """Allocate fixed-size, reference-counted pages from shared K/V pools.
+
+    The drop-in for hayate's ``PagedKVCacheManager`` (``hayate/engine/paged_cache.py:74-304``):
+    same constructor, methods (``allocate``, ``reserve``, ``truncate``, ``release``,
+    ``allocate_for_request``, ``import_cache``, ``snapshot``, ``begin_batch``,
+    ``commit_batch``), free-list order and exceptions, plus ``share`` (prefix pages aliased
+    with reference counts, copy-on-write on append). Pools are ``[layers, 1, H_kv,
+    capacity, head_dim]`` device tensors; ``begin_batch`` returns a ``PagedKVBatch`` whose
+    ``write_layer`` / ``attend_layer`` (and ``write_attend_layer``, ``prepare_layer``) run
+    this package's kernels.
+
+    Tuning attributes: ``kernel`` pins one attention kernel ("auto" lets the library
+    choose), ``split_tokens`` the decode split size (0: the library's), ``prefill_plan``
+    turns the prefill schedule on or off and ``prefill_max_splits`` bounds how many items a
+    schedule may cut in two. ``check_device_errors()`` raises if a kernel refused input.
+    """
 
     def __init__(self, num_layers: int, num_kv_heads: int, head_dim: int, max_cache_tokens: int,
                  page_size: int, max_requests: int, dtype: torch.dtype,
