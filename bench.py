@@ -50,7 +50,8 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default 2000; config 5's 128 for --workload longdecode)")
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["decode", "prefill", "longdecode", "engine"], default="decode")
@@ -65,7 +66,10 @@ def parse_args():
                     help="prefill workload: prefixes drawn from U[0, prefix-max] (config 3: 4096)")
     ap.add_argument("--reference-gpu", action="store_true",
                     help="also time the reference's compiled FlexAttention path on the GPU (needs baseline/_ref)")
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 128 if args.workload == "longdecode" else 2000
+    return args
 
 
 def load_peaks():
