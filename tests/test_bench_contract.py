@@ -1,0 +1,41 @@
+"""bench.py's reference arm runs on the host cores and prints the driver's JSON line
+(CPU only: the oracle port on a bounded sample)."""
+
+from __future__ import annotations
+
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_reference_arm_prints_the_contract_line():
+    proc = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1",
+                           "--warmup", "0"], cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    line = json.loads(proc.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference"
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config"):
+        assert key in line, key
+    assert line["metric"] == "decode attn HBM GB/s (% of peak)" and line["unit"] == "GB/s"
+    assert line["value"] > 0 and line["steps"] == 1
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
+
+
+def test_longdecode_defaults_to_config5_steps():
+    sys.path.insert(0, ROOT)
+    import bench
+
+    old = sys.argv
+    try:
+        sys.argv = ["bench.py", "--workload", "longdecode"]
+        assert bench.parse_args().steps == 128
+        sys.argv = ["bench.py"]
+        assert bench.parse_args().steps == 2000
+    finally:
+        sys.argv = old
