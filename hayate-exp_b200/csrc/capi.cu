@@ -530,18 +530,29 @@ constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
 void* g_scratch_addr[kMaxDevices] = {};
 
-// Device address of g_decode_scratch on the current device (looked up once per device).
-int decode_scratch_address(void** out) {
+// Device address of g_decode_scratch on the current device. Looked up afresh on every
+// call made outside stream capture (cheap), so a context re-created after
+// cudaDeviceReset gets its own address; a call made while `stream` is being captured
+// uses the address the last uncaptured call on this device found (and fails if there
+// was none).
+int decode_scratch_address(cudaStream_t stream, void** out) {
   int device = 0;
   cudaError_t err = cudaGetDevice(&device);
   if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
   if (device < 0 || device >= kMaxDevices) return fail(HYT_ERR_UNSUPPORTED, "device index too large");
+  cudaStreamCaptureStatus status = cudaStreamCaptureStatusNone;
+  err = cudaStreamIsCapturing(stream, &status);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaStreamIsCapturing");
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_addr[device] == nullptr) {
+  if (status == cudaStreamCaptureStatusNone) {
     void* addr = nullptr;
     err = cudaGetSymbolAddress(&addr, g_decode_scratch);
     if (err != cudaSuccess) return cuda_fail(err, "cudaGetSymbolAddress(decode scratch)");
     g_scratch_addr[device] = addr;
+  } else if (g_scratch_addr[device] == nullptr) {
+    return fail(HYT_ERR_INVALID,
+                "hyt_decode_attention_noalloc: the first call on a device must come before any "
+                "stream capture (it looks the static scratch's address up)");
   }
   *out = g_scratch_addr[device];
   return HYT_OK;
@@ -742,7 +753,7 @@ int hyt_decode_attention_noalloc(const void* q, const int64_t* q_strides, const 
                     std::to_string(HYT_NOALLOC_SCRATCH_BYTES) +
                     "-byte buffer; pass a larger split_tokens or use hyt_decode_attention");
   void* scratch = nullptr;
-  rc = decode_scratch_address(&scratch);
+  rc = decode_scratch_address(static_cast<cudaStream_t>(stream), &scratch);
   if (rc != HYT_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (L.total > 0) {

@@ -6,7 +6,7 @@ kernels (page-table KV scatter, tcgen05 chunked prefill, split-KV decode)
 through the C ABI of ``libhayate_b200.so``.
 """
 
-from .cache import Cache
+from .cache import Cache, KVSnapshot
 from .paged_cache import (
     MIN_KV_PAGE_SIZE,
     PagedCacheHandle,
@@ -18,6 +18,7 @@ from . import ops
 
 __all__ = [
     "Cache",
+    "KVSnapshot",
     "MIN_KV_PAGE_SIZE",
     "PagedCacheHandle",
     "PagedKVBatch",

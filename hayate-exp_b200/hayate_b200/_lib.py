@@ -13,6 +13,9 @@ import threading
 from ._build import LIB_PATH
 
 HYT_OK = 0
+HYT_ERR_INVALID, HYT_ERR_UNSUPPORTED, HYT_ERR_CUDA, HYT_ERR_WORKSPACE = -1, -2, -3, -4
+# size of the static scratch array of hyt_decode_attention_noalloc (include/hayate_b200.h)
+HYT_NOALLOC_SCRATCH_BYTES = 8 << 20
 HYT_DTYPE_BF16, HYT_DTYPE_F16, HYT_DTYPE_F32 = 0, 1, 2
 DEVICE_ERRORS = {
     1: "page id outside the pool",

@@ -1,10 +1,17 @@
-"""Contiguous per-request K/V snapshot, the exchange type of ``import_cache``/``snapshot``.
+"""An immutable K/V snapshot of one request, the value exchanged with hayate's engine.
 
-Same interface as hayate's ``Cache`` (``hayate/model/cache.py:6-83``): tensors of
-shape ``[layers, KV heads, tokens, head_dim]``, ``length``/``capacity``,
-``from_tensors``, ``append``, ``slice`` and ``reset``. Any object exposing
-``k``, ``v`` and ``length`` (the reference's own ``Cache`` included) is accepted
-where one is expected.
+``PagedKVCacheManager.snapshot`` returns one and ``import_cache`` /
+``allocate_for_request`` accept one. hayate only ever reads ``k``, ``v`` and
+``length`` from it and takes prefixes with ``slice(end, clone)``: the engine stores
+a prompt's snapshot in its prefix cache (``hayate/engine/engine.py:188-198``), the
+prefix cache keeps a cloned prefix of it and hands out uncloned prefixes on a hit
+(``hayate/engine/prefix_cache.py:57-80``), and the manager copies a hit back into
+pages (``hayate/engine/paged_cache.py:142-166``). A snapshot is finished when it is
+made, so this type is a read-only view: no in-place growth, no reset. ``extended``
+returns a new, longer snapshot for the rare caller that needs one.
+
+Any object with ``k``, ``v`` and ``length`` (hayate's own ``Cache`` included) is
+accepted wherever a snapshot is expected.
 """
 
 from __future__ import annotations
@@ -12,61 +19,67 @@ from __future__ import annotations
 import torch
 
 
-class Cache:
-    __slots__ = ("k", "v", "_length")
+class KVSnapshot:
+    """K and V of ``length`` tokens as ``[layers, kv_heads, tokens, head_dim]`` tensors
+    (both ``None`` for an empty snapshot). The tensors are shared, not copied, unless a
+    method says otherwise."""
 
-    def __init__(self):
-        self.k: torch.Tensor | None = None
-        self.v: torch.Tensor | None = None
-        self._length = 0
+    __slots__ = ("_k", "_v")
+
+    def __init__(self, k: torch.Tensor | None = None, v: torch.Tensor | None = None):
+        if (k is None) != (v is None):
+            raise ValueError("a snapshot holds both K and V or neither")
+        if k is not None:
+            if k.dim() != 4:
+                raise ValueError(f"snapshot tensors are [layers, kv_heads, tokens, head_dim], got {tuple(k.shape)}")
+            if k.shape != v.shape:
+                raise ValueError(f"snapshot K {tuple(k.shape)} and V {tuple(v.shape)} differ in shape")
+        self._k, self._v = k, v
 
     @classmethod
-    def from_tensors(cls, k: torch.Tensor | None, v: torch.Tensor | None) -> "Cache":
-        cache = cls()
-        cache.k, cache.v = k, v
-        cache._length = 0 if k is None else k.shape[2]
-        return cache
+    def from_tensors(cls, k: torch.Tensor | None, v: torch.Tensor | None) -> "KVSnapshot":
+        """Wrap existing tensors (no copy); the token count is their third dimension."""
+        return cls(k, v)
+
+    @property
+    def k(self) -> torch.Tensor | None:
+        return self._k
+
+    @property
+    def v(self) -> torch.Tensor | None:
+        return self._v
 
     @property
     def length(self) -> int:
-        return self._length
+        return 0 if self._k is None else int(self._k.shape[2])
 
-    @property
-    def capacity(self) -> int:
-        return 0 if self.k is None else self.k.shape[2]
+    # a snapshot is exactly as long as it is: no spare room to grow into
+    capacity = length
 
-    def append(self, k: torch.Tensor, v: torch.Tensor, capacity: int | None = None) -> None:
-        if k.shape != v.shape:
-            raise ValueError("key and value cache tensors must have matching shapes")
-        added = k.shape[2]
-        if added == 0:
-            return
-        need = self._length + added
-        if self.k is None or self.v is None or self.capacity < need:
-            grown = max(need, capacity or 0, max(1, 2 * self.capacity))
-            shape = (k.shape[0], k.shape[1], grown, k.shape[3])
-            new_k = torch.empty(shape, dtype=k.dtype, device=k.device)
-            new_v = torch.empty(shape, dtype=v.dtype, device=v.device)
-            if self.k is not None and self.v is not None and self._length:
-                new_k[:, :, : self._length].copy_(self.k[:, :, : self._length])
-                new_v[:, :, : self._length].copy_(self.v[:, :, : self._length])
-            self.k, self.v = new_k, new_v
-        self.k[:, :, self._length : need].copy_(k)
-        self.v[:, :, self._length : need].copy_(v)
-        self._length = need
-
-    def slice(self, end: int, clone: bool = False) -> "Cache":
-        if end < 0:
-            raise ValueError("cache slice end must be non-negative")
-        if self.k is None or self.v is None:
-            return Cache()
-        if end > self.length:
-            raise ValueError(f"cache slice end {end} exceeds cache length {self.length}")
-        k, v = self.k[:, :, :end], self.v[:, :, :end]
+    def slice(self, end: int, clone: bool = False) -> "KVSnapshot":
+        """The first ``end`` tokens: a view of these tensors, or compact copies if ``clone``
+        (what a prefix cache stores, so later writes to the source cannot reach it)."""
+        if not 0 <= end <= self.length:
+            raise ValueError(f"prefix of {end} tokens requested from a {self.length}-token snapshot")
+        if self._k is None:
+            return KVSnapshot()
+        k, v = self._k[:, :, :end], self._v[:, :, :end]
         if clone:
-            k, v = k.contiguous().clone(), v.contiguous().clone()
-        return Cache.from_tensors(k, v)
+            k, v = k.clone(memory_format=torch.contiguous_format), v.clone(memory_format=torch.contiguous_format)
+        return KVSnapshot(k, v)
 
-    def reset(self) -> None:
-        self.k = self.v = None
-        self._length = 0
+    def extended(self, k: torch.Tensor, v: torch.Tensor) -> "KVSnapshot":
+        """A new snapshot with ``k``/``v`` (same layers, heads and head_dim) after these
+        tokens. It is one exact-size concatenation: growing token by token this way costs
+        a full copy per call, which is why snapshots are made once, from the pages."""
+        if self._k is None:
+            return KVSnapshot(k, v)
+        return KVSnapshot(torch.cat([self._k, k], dim=2), torch.cat([self._v, v], dim=2))
+
+    def __repr__(self) -> str:
+        shape = None if self._k is None else tuple(self._k.shape)
+        return f"KVSnapshot(length={self.length}, shape={shape})"
+
+
+# hayate's name for the exchange type (``hayate/model/cache.py``), kept for drop-in use
+Cache = KVSnapshot

@@ -46,7 +46,7 @@ import numpy as np
 import torch
 
 from . import ops
-from .cache import Cache
+from .cache import KVSnapshot
 
 MIN_KV_PAGE_SIZE = 128  # hayate/engine/constants.py:27 (FlexAttention block size floor)
 
@@ -594,7 +594,7 @@ class PagedKVCacheManager:
             self._rows.set_row(handle.slot, handle.pages)
         handle.length = length
 
-    def snapshot(self, handle: PagedCacheHandle, length: int | None = None) -> Cache:
+    def snapshot(self, handle: PagedCacheHandle, length: int | None = None) -> KVSnapshot:
         """Gather a compact ``[layers, H_kv, length, D]`` copy of a request's cache."""
         if handle.released:
             raise RuntimeError("cannot snapshot a released cache handle")
@@ -604,7 +604,7 @@ class PagedKVCacheManager:
         slots = self._physical_positions(handle, n)
         k = self.k_cache[:, 0].index_select(2, slots).contiguous()
         v = self.v_cache[:, 0].index_select(2, slots).contiguous()
-        return Cache.from_tensors(k, v)
+        return KVSnapshot(k, v)
 
     def release(self, handle: PagedCacheHandle) -> None:
         """Drop a request's pages and return its slot."""
@@ -646,6 +646,19 @@ class PagedKVCacheManager:
         # (a decode step inside its last page needs none: the common case stays cheap)
         growing = [(h, n) for h, n in zip(handles, kv_lengths) if n > len(h.pages) * size]
         extra = sum(-(-n // size) - len(h.pages) for h, n in growing)
+        # plus the pages copy-on-write will take, so that a step that cannot get all of its
+        # pages fails here, before any reservation or copy: a held page with r holders that
+        # w of this batch's requests append into is copied min(w, r - 1) times (once the
+        # others have their copies, the last writer holds it alone)
+        writers: dict[int, int] = {}
+        for handle, length, n in zip(handles, lengths, query_lens):
+            if handle.aliased:
+                held_end = min(length + n, len(handle.pages) * size)  # appends into held pages
+                for logical in range(length // size, -(-held_end // size)):
+                    page = handle.pages[logical]
+                    if self._page_refs[page] > 1:
+                        writers[page] = writers.get(page, 0) + 1
+        extra += sum(min(w, int(self._page_refs[page]) - 1) for page, w in writers.items())
         if extra > len(self._free_pages):
             raise MemoryError(
                 f"paged KV cache is full: batch needs {extra} additional pages, "

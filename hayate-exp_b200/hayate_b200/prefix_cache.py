@@ -1,20 +1,20 @@
-"""Prefix cache that shares physical KV pages instead of copying them.
+"""Prefix cache whose entries alias physical KV pages instead of holding copies.
 
-Same interface and LRU policy as hayate's ``PrefixCache``
-(``hayate/engine/prefix_cache.py:18-100``): ``get(tokens, max_prefix_len)``
-returns the longest cached prefix, ``put(tokens, source)`` stores one within a
-token budget (least recently used entries are evicted first), ``clear()`` drops
-everything. The difference is what an entry holds: the reference clones a
-contiguous K/V snapshot on ``put`` and copies it back into fresh pages on a hit
-(``paged_cache.py:153-190``); here an entry is a page-aliasing handle
-(``PagedKVCacheManager.share``), so ``put`` and a hit cost no K/V traffic at all
-and a hit's pages are shared until the new request writes into them.
+It offers the calls hayate's ``PrefixCache`` offers (``hayate/engine/prefix_cache.py:18-100``):
+``get(tokens, max_prefix_len)`` finds the longest stored prefix of a prompt, ``put(tokens,
+source)`` stores one under a token budget with least-recently-used eviction, ``clear()``
+empties it. What an entry is differs. hayate clones a contiguous K/V snapshot on ``put``
+and copies it back into fresh pages on a hit (``hayate/engine/paged_cache.py:153-190``).
+Here an entry is a handle made by ``PagedKVCacheManager.share``: it holds references on
+the source's pages, so ``put`` and a hit move no K/V bytes, and a hit's pages stay shared
+until the new request writes into one of them (copy-on-write in ``begin_batch``).
 """
 
 from __future__ import annotations
 
 from collections import OrderedDict
 from dataclasses import dataclass
+from itertools import takewhile
 from typing import Sequence
 
 from .paged_cache import PagedCacheHandle, PagedKVCacheManager
@@ -22,81 +22,86 @@ from .paged_cache import PagedCacheHandle, PagedKVCacheManager
 
 @dataclass(frozen=True)
 class PrefixCacheMatch:
-    """Cached token count and a fresh request handle aliasing those tokens' pages."""
+    """How many leading tokens were found, and a new handle aliasing their pages."""
 
     length: int
     handle: PagedCacheHandle | None
 
 
+_MISS = PrefixCacheMatch(0, None)
+
+
+def _shared_prefix_len(a: Sequence[int], b: Sequence[int], cap: int) -> int:
+    """Number of equal leading tokens of ``a`` and ``b``, at most ``cap``."""
+    return sum(1 for _ in takewhile(lambda pair: pair[0] == pair[1], zip(a[:cap], b[:cap])))
+
+
 class PagedPrefixCache:
-    """LRU map from token prefixes to page-aliasing handles of one manager."""
+    """Token-prefix -> page-aliasing handle map of one manager, evicted oldest-use first.
+
+    Every entry owns its handle: eviction, replacement and ``clear`` release it, which
+    drops the entry's references on the pages (a page is freed once no request or entry
+    references it).
+    """
 
     def __init__(self, manager: PagedKVCacheManager, max_tokens: int):
         if max_tokens < 0:
-            raise ValueError("prefix cache token budget must be non-negative")
+            raise ValueError(f"max_tokens is a token budget and cannot be negative (got {max_tokens})")
         self.manager = manager
         self.max_tokens = max_tokens
         self.total_tokens = 0
+        # least recently used first; a hit or a store moves the entry to the end
         self._entries: OrderedDict[tuple[int, ...], PagedCacheHandle] = OrderedDict()
 
     def get(self, tokens: Sequence[int], max_prefix_len: int | None = None) -> PrefixCacheMatch:
-        """Longest cached prefix of ``tokens``; on a hit a NEW handle shares its pages.
+        """The longest stored prefix of ``tokens`` (at most ``max_prefix_len`` long).
 
-        The caller owns the returned handle (release it like any other request).
+        On a hit the match carries a NEW handle sharing that prefix's pages; the caller owns
+        it and releases it like any request handle. Ties keep the first entry found.
         """
-        if self.max_tokens == 0 or not tokens or not self._entries:
-            return PrefixCacheMatch(0, None)
-        key = tuple(tokens)
-        limit = len(key) if max_prefix_len is None else min(len(key), max_prefix_len)
-        if limit <= 0:
-            return PrefixCacheMatch(0, None)
-        best, best_len = None, 0
-        for cached, handle in self._entries.items():
-            n = _common_prefix(key, cached, limit)
-            if n > best_len and n <= handle.length:
-                best, best_len = cached, n
-                if best_len == limit:
+        if not tokens or not self._entries or self.max_tokens == 0:
+            return _MISS
+        prompt = tuple(tokens)
+        cap = len(prompt) if max_prefix_len is None else min(len(prompt), max_prefix_len)
+        if cap < 1:
+            return _MISS
+        hit_key, hit_len = None, 0
+        for key, entry in self._entries.items():
+            # an entry can only serve as many tokens as its handle still holds
+            n = _shared_prefix_len(prompt, key, min(cap, entry.length))
+            if n > hit_len:
+                hit_key, hit_len = key, n
+                if n == cap:  # nothing can beat a full-length match
                     break
-        if best is None:
-            return PrefixCacheMatch(0, None)
-        self._entries.move_to_end(best)
-        return PrefixCacheMatch(best_len, self.manager.share(self._entries[best], best_len))
+        if hit_key is None:
+            return _MISS
+        self._entries.move_to_end(hit_key)
+        return PrefixCacheMatch(hit_len, self.manager.share(self._entries[hit_key], hit_len))
 
     def put(self, tokens: Sequence[int], source: PagedCacheHandle) -> None:
-        """Remember ``tokens``' prefix as held by ``source`` (aliases its pages, no copy)."""
-        if self.max_tokens == 0 or not tokens or source.length == 0:
-            return
-        n = min(len(tokens), source.length, self.max_tokens)
-        if n <= 0:
+        """Store the longest prefix of ``tokens`` that ``source`` holds and the budget allows,
+        as an alias of ``source``'s pages (no copy). A key stored before is replaced."""
+        n = min(len(tokens), source.length, self.max_tokens) if tokens else 0
+        if n < 1:
             return
         key = tuple(tokens[:n])
-        entry = self.manager.share(source, n)
-        old = self._entries.pop(key, None)
-        if old is not None:
-            self.total_tokens -= len(key)
-            self.manager.release(old)
-        self._entries[key] = entry
-        self.total_tokens += len(key)
-        self._evict()
+        alias = self.manager.share(source, n)
+        replaced = self._entries.pop(key, None)
+        if replaced is not None:
+            self._drop(key, replaced)
+        self._entries[key] = alias
+        self.total_tokens += n
+        while self.total_tokens > self.max_tokens and self._entries:
+            self._drop(*self._entries.popitem(last=False))
 
     def clear(self) -> None:
-        for handle in self._entries.values():
-            self.manager.release(handle)
-        self._entries.clear()
-        self.total_tokens = 0
+        """Release every entry's handle and forget all prefixes."""
+        while self._entries:
+            self._drop(*self._entries.popitem())
 
     def __len__(self) -> int:
         return len(self._entries)
 
-    def _evict(self) -> None:
-        while self.total_tokens > self.max_tokens and self._entries:
-            key, handle = self._entries.popitem(last=False)
-            self.total_tokens -= len(key)
-            self.manager.release(handle)
-
-
-def _common_prefix(left: Sequence[int], right: Sequence[int], limit: int) -> int:
-    n, top = 0, min(len(left), len(right), limit)
-    while n < top and left[n] == right[n]:
-        n += 1
-    return n
+    def _drop(self, key: tuple[int, ...], handle: PagedCacheHandle) -> None:
+        self.total_tokens -= len(key)
+        self.manager.release(handle)

@@ -145,10 +145,14 @@ int hyt_decode_attention(const void* q, const int64_t* q_strides, const void* k_
  * HYT_NOALLOC_SCRATCH_BYTES that every GPU loading this library holds until
  * the process exits. Sizes whose workspace (hyt_attention_workspace_bytes)
  * exceeds it are refused with HYT_ERR_WORKSPACE; a larger split_tokens needs
- * less. The first call on a device looks the array's address up (once per
- * device), so make that first call before any stream capture. Every call
- * clears the counter area on `stream` and then reuses the array, so calls
- * that overlap on the GPU (other streams, other threads) race on it.
+ * less. Every call made outside stream capture looks the array's address up
+ * on the current device (so a context re-created after cudaDeviceReset gets
+ * the new address); a call made while `stream` is being captured reuses the
+ * address its device's last uncaptured call found, so make the first call on
+ * each device before any stream capture (a captured first call is refused
+ * with HYT_ERR_INVALID). Every call clears the counter area on `stream` and
+ * then reuses the array, so calls that overlap on the GPU (other streams,
+ * other threads) race on it.
  */
 #define HYT_NOALLOC_SCRATCH_BYTES (8u << 20)
 int hyt_decode_attention_noalloc(const void* q, const int64_t* q_strides, const void* k_pool,

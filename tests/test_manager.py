@@ -271,3 +271,38 @@ def test_copy_on_write_follows_sharing_only():
     assert a.pages[0] == twin.pages[0] and manager.page_refcount(a.pages[0]) == 2
     manager.release(twin)
     assert not twin.aliased
+
+
+def test_copy_on_write_pages_counted_before_any_change():
+    """A step whose growth fits but whose copy-on-write pages do not fails up front: no
+    handle gains a page and no reference count moves."""
+    manager = PagedKVCacheManager(1, 1, 4, 6 * 128, 128, 6, torch.float32, "cpu")
+    values = torch.randn(1, 1, 200, 4)
+    src = manager.allocate_for_request(Cache.from_tensors(values, values))   # pages 0, 1
+    twins = [manager.share(src, 200) for _ in range(3)]                      # page 1 held by 4
+    grow = manager.allocate_for_request(Cache.from_tensors(values[:, :, :128], values[:, :, :128]))
+    assert len(manager._free_pages) == 3
+    # grow needs 1 new page; the 3 twins each append into page 1 (4 holders): 3 copies
+    handles = [grow] + twins
+    before = ([list(h.pages) for h in handles], manager._page_refs.copy(), list(manager._free_pages))
+    with pytest.raises(MemoryError):
+        manager.begin_batch(handles, 1)
+    assert [list(h.pages) for h in handles] == before[0]
+    assert np.array_equal(manager._page_refs, before[1]) and manager._free_pages == before[2]
+    # without the growing request the three copies fit exactly, and the last writer keeps
+    # nothing shared: src still holds the original page alone
+    manager.begin_batch(twins, 1)
+    assert len(manager._free_pages) == 0
+    assert manager.page_refcount(src.pages[1]) == 1
+    assert len({t.pages[1] for t in twins} | {src.pages[1]}) == 4
+
+
+def test_copy_on_write_count_is_exact_when_all_holders_write():
+    """Every holder of a page writing into it needs one copy fewer than holders."""
+    manager = PagedKVCacheManager(1, 1, 4, 4 * 128, 128, 4, torch.float32, "cpu")
+    values = torch.randn(1, 1, 200, 4)
+    src = manager.allocate_for_request(Cache.from_tensors(values, values))   # pages 0, 1
+    twin = manager.share(src, 200)
+    assert len(manager._free_pages) == 2
+    manager.begin_batch([src, twin], 1)  # page 1 has 2 holders, both write: 1 copy
+    assert len(manager._free_pages) == 1 and src.pages[1] != twin.pages[1]
