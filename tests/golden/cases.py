@@ -59,8 +59,25 @@ CASES = (
 )
 
 
+# Cases run through the reference's own GPU path (its torch.compile'd FlexAttention, bf16)
+# by ``make_reference_gpu.py`` on a B200; the tests compare this repository's kernels with
+# the stored rows on boxes where the reference is not installed.
+GPU_CASES = (
+    # decode, ragged histories across page edges (one split and several per request)
+    Case("refgpu_decode", 1, 0, 32, 8, 128, 128, 8192, (1000, 4095, 129, 2048), 1, 31),
+    # four new tokens per request: the decode kernel's 16-row tile (4 heads x 4 tokens)
+    Case("refgpu_decode_t4", 1, 0, 32, 8, 128, 128, 2048, (127, 128, 300, 1), 4, 37),
+    # a prefill chunk over an empty, a short and a long prefix
+    Case("refgpu_prefill", 1, 0, 32, 8, 128, 128, 4096, (0, 300, 1500), 40, 41),
+    # a long and a short prefix, a chunk crossing a page edge, sharper scores (two requests:
+    # the reference's compiled FlexAttention fails to lower for a one-request batch on B200,
+    # Inductor NoValidChoicesError)
+    Case("refgpu_prefill_long", 1, 0, 32, 8, 128, 128, 4096, (2500, 700), 64, 43, 4.0),
+)
+
+
 def case_by_name(name: str) -> Case:
-    for case in CASES:
+    for case in CASES + GPU_CASES:
         if case.name == name:
             return case
     raise KeyError(name)

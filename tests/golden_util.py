@@ -13,7 +13,7 @@ GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 if GOLDEN_DIR not in sys.path:
     sys.path.insert(0, GOLDEN_DIR)
 
-from cases import CASES, case_by_name, make_inputs, shuffled_free_pages  # noqa: E402,F401
+from cases import CASES, GPU_CASES, case_by_name, make_inputs, shuffled_free_pages  # noqa: E402,F401
 
 
 def load_golden(name: str) -> dict:

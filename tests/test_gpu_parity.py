@@ -115,22 +115,44 @@ def test_decode_is_deterministic_and_leaves_counters_zero():
     assert ws is not None and int(ws[:256].view(torch.int32).abs().sum()) == 0
 
 
+def oracle_request_rows(manager, batch, q, requests, layer=0):
+    """The oracle's rows for some requests, each computed on a compact copy of only that
+    request's pages (host memory stays bounded at full config sizes)."""
+    table = batch.page_table.cpu().numpy().astype(np.int64)
+    lens = batch.cache_lens.cpu().numpy()
+    P, T = manager.page_size, q.shape[2]
+    H, D = manager.num_kv_heads, manager.head_dim
+    rows = {}
+    for b in requests:
+        n = -(-(int(lens[b]) + T) // P)
+        pages = torch.from_numpy(table[b, :n]).to(q.device)
+        pools = []
+        for pool in (manager.k_cache, manager.v_cache):
+            paged = pool[layer, 0].view(H, manager.num_pages, P, D)
+            pools.append(paged.index_select(1, pages).reshape(1, 1, H, n * P, D).float().cpu().numpy())
+        rows[b] = oracle.paged_attention(q[b:b + 1].float().cpu().numpy(), pools[0], pools[1], 0,
+                                         np.arange(n, dtype=np.int64)[None], lens[b:b + 1], P)[0]
+    return rows
+
+
 def test_full_size_decode_sweep_config():
-    """Config 2 shapes (B=64, kv 1024..8192): decode vs the CUDA-core kernel, plus an oracle sample."""
+    """Config 2 shapes (B=64, kv 1024..8192, shuffled pages): every request against the oracle,
+    through the one-launch decode step (the kernel writes the new rows itself)."""
     rng = np.random.RandomState(0)
     lengths = [int(n) - 1 for n in rng.randint(1024, 8193, size=64)]
     manager, _, batch, q, k, v = build_step(lengths, 1, seed=11)
-    batch.write_layer(0, k, v)
-    out = batch.attend_layer(q, 0)
-    manager.kernel = "generic"
-    ref_gpu = batch.attend_layer(q, 0)
+    out = batch.write_attend_layer(0, k, v, q)
     torch.cuda.synchronize()
     manager.check_device_errors()
-    assert (out.float() - ref_gpu.float()).abs().max().item() <= 2e-2
-    sample = [0, 17, 63]
-    ref = oracle_out(manager, batch, q, requests=sample)
-    err = np.abs(out.float().cpu().numpy()[sample] - ref[sample]).max()
+    got = out.float().cpu().numpy()
+    ref = oracle_request_rows(manager, batch, q, range(64))
+    err = max(float(np.abs(got[b] - ref[b]).max()) for b in range(64))
     assert err <= 2e-2, err
+    # the rows the step wrote are the step's k/v, bit for bit
+    table, lens = batch.page_table.long(), batch.cache_lens
+    slots = table[torch.arange(64, device="cuda"), lens // 128] * 128 + lens % 128
+    assert torch.equal(manager.k_cache[0, 0][:, slots], k[:, :, 0].transpose(0, 1))
+    assert torch.equal(manager.v_cache[0, 0][:, slots], v[:, :, 0].transpose(0, 1))
 
 
 @pytest.mark.parametrize("query_len", [1, 7, 130])
@@ -234,21 +256,32 @@ def test_prefill_contiguous_q_and_multi_layer():
     assert err <= 2e-2, err
 
 
-def test_full_size_prefill_config():
-    """Config 3 shapes (8 requests x 512-token chunk on prefixes U[0, 4096])."""
+@pytest.mark.parametrize("plan", [False, True], ids=["default_grid", "planned"])
+def test_full_size_prefill_config(plan):
+    """Config 3 shapes (8 requests x 512-token chunk on prefixes U[0, 4096]): every request
+    against the oracle, on the default grid and on a planned schedule with items cut in two."""
     rng = np.random.RandomState(1)
     prefixes = [int(n) for n in rng.randint(0, 4097, size=8)]
     manager, _, batch, q, k, v = build_step(prefixes, 512, seed=21)
+    if plan:
+        # a near-free merge cost makes the planner cut its heaviest items in two
+        items, splits = ops.prefill_plan(prefixes, 512, 32, manager.num_sms, 128, item_overhead=5.0,
+                                         merge_cost=0.01)
+        assert items is not None and splits > 0
     batch.write_layer(0, k, v)
-    out = batch.attend_layer(q, 0)  # auto: the tcgen05 prefill kernel
-    manager.kernel = "generic"
-    ref_gpu = batch.attend_layer(q, 0)
+    if plan:
+        out = ops.prefill_attention_planned(
+            q, manager.k_cache, manager.v_cache, 0, batch.page_table, batch.cache_lens_i32, 128,
+            torch.from_numpy(items.reshape(-1)).to("cuda").view(-1, 4), splits,
+            workspace=manager.prefill_workspace(splits), error_word=manager.error_word)
+    else:
+        manager.prefill_plan = False
+        out = batch.attend_layer(q, 0)  # auto: the tcgen05 prefill kernel, default grid
     torch.cuda.synchronize()
     manager.check_device_errors()
-    assert (out.float() - ref_gpu.float()).abs().max().item() <= 2e-2
-    sample = [0, 5]
-    ref = oracle_out(manager, batch, q, requests=sample)
-    err = np.abs(out.float().cpu().numpy()[sample] - ref[sample]).max()
+    got = out.float().cpu().numpy()
+    ref = oracle_request_rows(manager, batch, q, range(8))
+    err = max(float(np.abs(got[b] - ref[b]).max()) for b in range(8))
     assert err <= 2e-2, err
 
 

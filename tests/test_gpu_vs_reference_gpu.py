@@ -1,9 +1,11 @@
 """Our kernels against the reference's own GPU attention (torch.compile'd FlexAttention).
 
-Runs only where the reference is installed in ``baseline/_ref`` (an offline pip
-install of hayate-exp); elsewhere the module is skipped. Inputs go through the
-reference's own ``allocate_for_request``/``begin_batch``/``write_layer``/
-``attend_layer``; its pools are zeroed first (it allocates them with torch.empty).
+Two forms. Live, where the reference is installed in ``baseline/_ref`` (an offline pip
+install of hayate-exp): inputs go through the reference's own ``allocate_for_request``/
+``begin_batch``/``write_layer``/``attend_layer`` on this GPU (its pools zeroed first: it
+allocates them with ``torch.empty``). Recorded, everywhere: the same reference path was
+run on a B200 by ``tests/golden/make_reference_gpu.py`` on exact-valued inputs, and its
+rows, page tables and pool digests are fixtures in ``tests/golden/refgpu_*.npz``.
 """
 
 from __future__ import annotations
@@ -15,7 +17,8 @@ import sys
 import pytest
 import torch
 
-from hayate_b200 import PagedKVCacheManager
+from golden_util import GPU_CASES, load_golden, make_inputs, shuffled_free_pages
+from hayate_b200 import KVSnapshot, PagedKVCacheManager
 from hayate_b200 import workloads as W
 
 pytestmark = pytest.mark.gpu
@@ -63,3 +66,37 @@ def test_matches_reference_gpu_attention(ref, lengths, query_len):
     torch.cuda.synchronize()
     ours.check_device_errors()
     assert (got.float() - expected.float()).abs().max().item() <= 2e-2
+
+
+def _bf16_digest(t: torch.Tensor) -> str:
+    import hashlib
+
+    return hashlib.sha256(t.contiguous().view(torch.int16).cpu().numpy().tobytes()).hexdigest()
+
+
+@pytest.mark.parametrize("case", GPU_CASES, ids=lambda c: c.name)
+def test_matches_recorded_reference_gpu_rows(case):
+    """The reference's GPU rows recorded on a B200: same page tables, bit-equal pools after
+    the write, attention within 2e-2."""
+    golden = load_golden(case.name)
+    inputs = make_inputs(case)
+    dev = lambda a: torch.from_numpy(a).to("cuda", torch.bfloat16)  # noqa: E731
+    m = PagedKVCacheManager(case.num_layers, case.num_kv_heads, case.head_dim, case.max_cache_tokens,
+                            case.page_size, case.batch, torch.bfloat16, "cuda")
+    m._free_pages = shuffled_free_pages(m.num_pages, case.seed)
+    hs = [m.allocate_for_request(KVSnapshot(dev(hk), dev(hv)) if hk.shape[2] else None)
+          for hk, hv in zip(inputs["hist_k"], inputs["hist_v"])]
+    batch = m.begin_batch(hs, case.query_len)
+    batch.write_layer(case.layer, dev(inputs["k_new"]), dev(inputs["v_new"]))
+    out = batch.attend_layer(dev(inputs["q"]), case.layer)
+    torch.cuda.synchronize()
+    m.check_device_errors()
+    table = golden["page_table"]
+    width = batch.page_table.shape[1]
+    assert (batch.page_table.cpu().numpy() == table[:, :width]).all() and (table[:, width:] == -1).all()
+    assert (batch.cache_lens.cpu().numpy() == golden["cache_lens"]).all()
+    assert _bf16_digest(m.k_cache) == str(golden["k_pool_sha256"])
+    assert _bf16_digest(m.v_cache) == str(golden["v_pool_sha256"])
+    expected = torch.from_numpy(golden["out_bf16"]).view(torch.bfloat16).float()
+    err = (out.float().cpu() - expected).abs().max().item()
+    assert err <= 2e-2, err
