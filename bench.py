@@ -20,9 +20,16 @@ Multi-GPU: one process per GPU (torchrun), each rank owns its own pool and
 requests; there is no collective on the data path. Timing is by CUDA events,
 max over ranks (NCCL all_reduce of the elapsed times only).
 
-``--impl reference`` times the CPU oracle (a NumPy restatement of hayate's
-paged attention, the reference being pure Python/PyTorch with no compiled
-path) on a bounded sample of the same workload with every host thread.
+The default run adds, beside the config-2 headline: config 3 (and the same shape
+on longer prefixes), config 5 at every N (its own 128 steps, with each rank's
+kernel time, host time and barrier wait), config 4's engine at N=1, the e2e
+number through the public API with host buffers, and the CPU baseline.
+
+``--impl reference`` times hayate's OWN CPU attention path (its unmodified
+``PagedKVCacheManager``/``PagedKVBatch`` from ``baseline/_ref``, fp32, eager
+FlexAttention) with every host thread, on a bounded sample of config 2 (and
+config 1 exactly beside it); the NumPy restatement stands in only where the
+reference cannot be imported.
 """
 
 from __future__ import annotations
@@ -60,6 +67,7 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="headline workload only")
+    ap.add_argument("--no-engine", action="store_true", help="skip the config-4 engine leg of the default run")
     ap.add_argument("--no-prefill-plan", action="store_true",
                     help="prefill on the default grid instead of the planned schedule")
     ap.add_argument("--prefix-max", type=int, default=4096,
@@ -108,66 +116,119 @@ def prefill_prefixes(seed: int, batch: int = 8, hi: int = 4096):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled in the background (read-only)."""
+    """SM clock and clock-event reasons sampled in the background while a leg runs
+    (read-only NVML queries every 10 ms; nvidia-smi if NVML is unavailable).
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    Samples are kept from ``__enter__`` to ``__exit__``. A leg's timed region can be a few
+    milliseconds (20 decode steps take ~4 ms), shorter than any sampling period, so each
+    leg calls ``hold(step)`` after its timed loop: the same step keeps the GPU busy for at
+    least ``min_s`` more seconds inside the window (untimed), and ``summary()`` reports
+    the samples of the whole window.
+    """
 
-    def __init__(self, gpu_index: int, period_ms: int = 50):
+    REASONS = (("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20), ("hw_thermal_slowdown", 0x40),
+               ("hw_power_brake_slowdown", 0x80), ("sw_power_cap", 0x4))
+    SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int, period_ms: int = 10):
         self.gpu_index = gpu_index
-        self.period_ms = period_ms
-        self.proc = None
-        self.lines: list[str] = []
-        self.thread = None
+        self.period_s = period_ms / 1e3
+        self.samples: list[tuple[float, set]] = []
+        self.max_mhz = None
+        self.source = None
+        self.held_s = 0.0
+        self._stop = threading.Event()
+        self._thread = None
+        self._proc = None
 
-    def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.gpu_index), "-lms", str(self.period_ms)],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-            deadline = time.time() + 3.0  # let nvidia-smi start so the timed region is sampled
-            while not self.lines and time.time() < deadline and self.proc.poll() is None:
-                time.sleep(0.02)
-            self.lines.clear()
-        except OSError:
-            self.proc = None
-        return self
+    def _nvml_handle(self):
+        import pynvml
+        import torch
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+        pynvml.nvmlInit()
+        try:  # the CUDA device's PCI address: NVML's index order can differ from CUDA's
+            props = torch.cuda.get_device_properties(self.gpu_index)
+            bus = "%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.gpu_index)
 
-    def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
+    def _poll_nvml(self, handle):
+        import pynvml
+
+        while not self._stop.is_set():
             try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-        if self.thread is not None:
-            self.thread.join(timeout=2)
+                mhz = float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM))
+                bits = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle))
+            except Exception:
+                break
+            self.samples.append((mhz, {name for name, bit in self.REASONS if bits & bit}))
+            self._stop.wait(self.period_s)
 
-    def summary(self):
-        sm, mx, reasons = [], None, set()
+    def _read_smi(self):
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        for line in self._proc.stdout:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
+                mhz, self.max_mhz = float(parts[1]), float(parts[2])
             except ValueError:
                 continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower().startswith("active"):
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+            self.samples.append((mhz, {n for n, f in zip(names, parts[5:9]) if f.lower().startswith("active")}))
+
+    def __enter__(self):
+        try:
+            import pynvml
+
+            handle = self._nvml_handle()
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+            self.source = "nvml"
+            self._thread = threading.Thread(target=self._poll_nvml, args=(handle,), daemon=True)
+        except Exception:
+            try:
+                self._proc = subprocess.Popen(
+                    ["nvidia-smi", f"--query-gpu={self.SMI_FIELDS}", "--format=csv,noheader,nounits",
+                     "-i", str(self.gpu_index), "-lms", "20"],
+                    stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self.source = "nvidia-smi"
+                self._thread = threading.Thread(target=self._read_smi, daemon=True)
+            except OSError:
+                return self
+        self._thread.start()
+        return self
+
+    def hold(self, step, min_s: float = 0.5) -> None:
+        """Run ``step()`` (untimed) until at least ``min_s`` seconds of GPU work have passed,
+        so the window holds samples taken under the leg's load."""
+        import torch
+
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < min_s:
+            for _ in range(8):
+                step()
+            torch.cuda.synchronize()
+        self.held_s = time.perf_counter() - t0
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
+
+    def summary(self):
+        sm = [mhz for mhz, _ in self.samples]
+        reasons = set().union(*[r for _, r in self.samples]) if self.samples else set()
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(sm), "source": self.source,
+                "window": "timed region + %.2f s of the same steps right after it" % self.held_s}
 
 
 # ---------------------------------------------------------------------------- distributed
@@ -309,6 +370,7 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
         end.record()
         torch.cuda.synchronize()
         barrier(world)
+        clocks.hold(step)
     ms_local = start.elapsed_time(end)
     kernel_ms = sum(a.elapsed_time(b) for a, b in kern) / args.steps
     manager.check_device_errors()
@@ -336,6 +398,7 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
     attn_ms = sum(a.elapsed_time(b) for a, b in attn) / n_unfused
     attn_gbs = kv_bytes / (attn_ms / 1e3) / 1e9
     manager.check_device_errors()
+    read_ceiling = plain_read_ceiling(kv_bytes, world)
 
     result = {
         "metric": "decode attn HBM GB/s (% of peak)",
@@ -370,10 +433,12 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
                      "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + write.sum)",
                      "bytes_per_launch": step_bytes,
                      "kernel": "decode_attention_kernel (split-KV decode with the fused row scatter)"},
+        "read_ceiling": read_ceiling,
         "gpu_launches": args.steps,
         "clocks": clocks.summary(),
         "output_checksums": [round(c, 6) for c in checksums],
     }
+    result["roofline"]["frac_of_read_ceiling"] = round(achieved / read_ceiling["GB_s"], 4)
     if args.reference_gpu and rank == 0:
         ref_gpu = reference_gpu_compare(manager, handles, q, k, v, out, kv_bytes / 1e9, "GB_s")
         if "ms" in ref_gpu:
@@ -385,6 +450,43 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline_decode(manager, batch, q, ctx)
     return result
+
+
+def plain_read_ceiling(nbytes: int, world: int, repeats: int = 20):
+    """HBM read ceiling on this GPU: the library's plain streaming-read kernel
+    (``hyt_read_probe``, 16-byte loads, 4 in flight per thread) over a contiguous buffer of
+    the decode step's KV size (> L2, so every launch reads HBM), best and mean of
+    ``repeats`` CUDA-event-timed launches, at the CTA count that reads fastest of a few."""
+    import torch
+
+    from hayate_b200 import ops
+
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    buf = torch.ones(nbytes // 16 * 16, dtype=torch.uint8, device="cuda")
+    best = {}
+    for per_sm in (2, 4, 8):
+        sink = torch.zeros(sms * per_sm, dtype=torch.int32, device="cuda")
+        for _ in range(3):
+            ops.read_probe(buf, sink)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(repeats)]
+        for a, b in evs:
+            a.record()
+            ops.read_probe(buf, sink)
+            b.record()
+        torch.cuda.synchronize()
+        ms = [a.elapsed_time(b) for a, b in evs]
+        best[per_sm] = (min(ms), sum(ms) / len(ms))
+    per_sm = min(best, key=lambda c: best[c][1])
+    ms_min, ms_mean = best[per_sm]
+    del buf
+    return {"GB_s": round(buf_gbs(nbytes, ms_mean), 1), "best_GB_s": round(buf_gbs(nbytes, ms_min), 1),
+            "bytes": nbytes // 16 * 16, "ctas": sms * per_sm,
+            "kernel": "read_probe_kernel (hyt_read_probe): contiguous 16-byte streaming loads, no writes",
+            "timing": f"mean (and best) of {repeats} launches, CUDA events, buffer > L2"}
+
+
+def buf_gbs(nbytes: int, ms: float) -> float:
+    return nbytes / (ms / 1e3) / 1e9
 
 
 def decode_e2e(args, world, manager, handles, ctx, q, k, v, step_bytes):
@@ -493,7 +595,112 @@ def cpu_threads() -> int:
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
 
 
-def cpu_baseline_decode(manager, batch, q, ctx, budget_s: float = 10.0):
+def import_reference():
+    """hayate's own modules from the offline install in ``baseline/_ref``, or the reason they
+    cannot be imported."""
+    if not os.path.isdir(os.path.join(REF_DIR, "hayate")):
+        return None, "the reference is not installed in baseline/_ref"
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    try:
+        import hayate.engine.paged_cache as paged_cache
+        from hayate.model.cache import Cache
+        from hayate.model.rope import apply_rope_vectorized, compute_rope_params
+
+        return (paged_cache, Cache, compute_rope_params, apply_rope_vectorized), None
+    except Exception as exc:  # pragma: no cover - depends on the box
+        return None, f"{type(exc).__name__}: {str(exc).splitlines()[0][:200]}"
+
+
+# The reference's CPU attention path on two workloads (fp32, its own manager and batch):
+# config 1 exactly, and a bounded sample of config 2 (its first 4 requests).
+REF_CPU_WORKLOADS = {
+    "config1": {"history": [511] * 4, "pool": 16384,
+                "what": "config 1: 4 requests x 512-token context (511 cached + 1 new), pool of 16384 "
+                        "slots in 128-token pages, fp32"},
+    "config2_sample": {"history": [n - 1 for n in decode_lengths(1000)[:4]], "pool": None,
+                       "what": "bounded sample of config 2: its first 4 requests (kv %s), pool sized to "
+                               "them plus 8 pages, fp32" % decode_lengths(1000)[:4]},
+}
+
+
+def reference_cpu_path(which: str, steps: int, warmup: int, budget_s: float | None = None):
+    """Time hayate's OWN paged attention path on the host cores: ``PagedKVCacheManager
+    .begin_batch -> PagedKVBatch.write_layer -> attend_layer`` (``hayate/engine/
+    paged_cache.py:202-293,44-71``), unmodified, in fp32 on the CPU. Its module-level
+    ``torch.compile(flex_attention)`` does not lower on the CPU (Inductor
+    LoweringException), so it is swapped for the eager ``flex_attention`` it wraps; the
+    attention math and masks are the reference's. Inputs: N(0,1), RMSNorm (QK-norm) and
+    the reference's own RoPE (theta 1e6) at true positions, seeded shuffled free pages.
+
+    One step is one layer's write + attention for the whole sample. ``value`` is GB/s of the
+    K/V rows attended, counted in fp32 (4 bytes per element, the dtype the reference runs
+    in). Timing stops early once ``budget_s`` seconds of steps are done."""
+    import random
+
+    import torch
+
+    mods, why = import_reference()
+    if mods is None:
+        return {"unavailable": why}
+    paged_cache, Cache, compute_rope_params, apply_rope = mods
+    from torch.nn.attention.flex_attention import flex_attention
+
+    paged_cache._compiled_flex_attention = flex_attention
+    threads = cpu_threads()
+    torch.set_num_threads(threads)
+    spec = REF_CPU_WORKLOADS[which]
+    hist = spec["history"]
+    B, HQ, HKV, D, P = len(hist), 32, 8, 128, 128
+    pool = spec["pool"] or (sum(math.ceil((n + 1) / P) for n in hist) + 8) * P
+    gen = torch.Generator().manual_seed(1)
+    cos, sin = compute_rope_params(D, 1_000_000, max(hist) + 2)
+
+    def qk(shape, pos):
+        x = torch.nn.functional.rms_norm(torch.randn(shape, generator=gen), (D,), eps=1e-6)
+        return apply_rope(x, cos, sin, pos)
+
+    import warnings
+
+    warnings.filterwarnings("ignore", message="flex_attention called without torch.compile")
+    with torch.inference_mode():
+        m = paged_cache.PagedKVCacheManager(1, HKV, D, pool, P, B, torch.float32, "cpu")
+        m.k_cache.zero_()
+        m.v_cache.zero_()
+        random.Random(0).shuffle(m._free_pages)
+        handles = []
+        for n in hist:
+            pos = torch.arange(n)[None]
+            k = qk((1, HKV, n, D), pos)
+            v = torch.randn((1, HKV, n, D), generator=gen)
+            handles.append(m.allocate_for_request(Cache.from_tensors(k, v)))  # [layers=1, H_kv, n, D]
+        pos = torch.tensor(hist)[:, None]
+        q, kn, vn = qk((B, HQ, 1, D), pos), qk((B, HKV, 1, D), pos), torch.randn((B, HKV, 1, D), generator=gen)
+        times = []
+        t_start = time.perf_counter()
+        for i in range(warmup + steps):
+            t0 = time.perf_counter()
+            batch = m.begin_batch(handles, 1)
+            batch.write_layer(0, kn, vn)
+            out = batch.attend_layer(q, 0)
+            dt = time.perf_counter() - t0
+            if i >= warmup:
+                times.append(dt)
+            if budget_s is not None and times and time.perf_counter() - t_start > budget_s:
+                break
+    kv_bytes = sum(n + 1 for n in hist) * HKV * D * 4 * 2
+    secs = sum(times)
+    return {"value": round(kv_bytes * len(times) / secs / 1e9, 4), "unit": "GB/s",
+            "ms_per_step": round(secs / len(times) * 1e3, 2), "steps_timed": len(times),
+            "cores": threads, "kind": "reference",
+            "sample": spec["what"] + "; one step = begin_batch + write_layer + attend_layer",
+            "path": "hayate PagedKVCacheManager.begin_batch -> PagedKVBatch.write_layer -> attend_layer "
+                    "(baseline/_ref, unmodified; eager flex_attention in place of its torch.compile "
+                    "wrapper, which does not lower on the CPU)",
+            "checksum": round(float(out.double().sum()), 6)}
+
+
+def cpu_port_decode(manager, batch, q, ctx, budget_s: float = 5.0):
     """The oracle (NumPy restatement of the reference path) on a bounded sample of requests."""
     import oracle
     from threadpoolctl import threadpool_limits
@@ -513,10 +720,22 @@ def cpu_baseline_decode(manager, batch, q, ctx, budget_s: float = 10.0):
             nbytes += ctx[r] * 8 * 128 * 2 * 2
             done += 1
     secs = time.perf_counter() - t0
-    return {"value": round(nbytes / secs / 1e9, 3), "unit": "GB/s", "cores": threads,
-            "kind": "port",
+    return {"value": round(nbytes / secs / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"{done} request-attentions cycling over the {len(ctx)}-request config-2 batch "
-                      f"(fp32 NumPy oracle on the same bf16-rounded inputs), {secs:.1f} s"}
+                      f"(fp32 NumPy oracle gathering only the attended keys, bf16 bytes counted), {secs:.1f} s"}
+
+
+def cpu_baseline_decode(manager, batch, q, ctx):
+    """The reference's own CPU path timed on the host cores (~10 s on a config-2 sample, ~6 s
+    on config 1), with the NumPy restatement's speed beside it."""
+    base = reference_cpu_path("config2_sample", steps=1000, warmup=2, budget_s=10.0)
+    if "unavailable" in base:  # no reference on this box: the restatement stands in
+        port = cpu_port_decode(manager, batch, q, ctx, budget_s=10.0)
+        port["reason"] = "reference not importable: " + base["unavailable"]
+        return port
+    base["config1"] = reference_cpu_path("config1", steps=1000, warmup=2, budget_s=6.0)
+    base["port"] = cpu_port_decode(manager, batch, q, ctx)
+    return base
 
 
 # ---------------------------------------------------------------------------- prefill (cfg 3)
@@ -568,6 +787,7 @@ def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=N
             evs[i][2].record()
         torch.cuda.synchronize()
         barrier(world)
+        clocks.hold(step)
     manager.check_device_errors()
     out = step()  # the rows (compared with the reference's when --reference-gpu)
     plan = batch.prefill_schedule(q)
@@ -607,7 +827,7 @@ def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=N
 
 
 # ---------------------------------------------------------------------------- long decode (cfg 5)
-LONG_GROUPS, LONG_PER_GROUP, LONG_PREFIX, LONG_CONTEXT = 32, 16, 4096, 32768
+LONG_GROUPS, LONG_PER_GROUP, LONG_PREFIX, LONG_CONTEXT, LONG_STEPS = 32, 16, 4096, 32768, 128
 
 
 def long_groups(rank: int, world: int) -> list[int]:
@@ -616,15 +836,22 @@ def long_groups(rank: int, world: int) -> list[int]:
     return [g for g in range(LONG_GROUPS) if g % world == rank]
 
 
-def run_longdecode(args, world, rank, local, peaks, peak_kind):
+def run_longdecode(args, world, rank, local, peaks, peak_kind, steps=None, warmup=None):
     """512 requests x 32768-token context, groups of 16 alias a 4096-token prefix (shared
-    pages); every request decodes one token per step. Groups are split across ranks."""
+    pages); every request decodes one token per step. Groups are split across ranks.
+
+    Besides tok/s (whole job, max over ranks) the leg reports, per rank and gathered in rank
+    order, what bounds the 1 -> N curve: the rank's decode-kernel time per step and its GB/s
+    of unique bytes, the host time of ``begin_batch`` per step, the rank's own elapsed time
+    and how long it waited at the closing barrier for the slowest rank."""
     import torch
 
     from hayate_b200 import PagedKVCacheManager
     from hayate_b200 import workloads as W
 
-    steps = args.steps
+    steps = args.steps if steps is None else steps
+    warmup = args.warmup if warmup is None else warmup
+    t_setup = time.perf_counter()
     groups = long_groups(rank, world)
     n_req = len(groups) * LONG_PER_GROUP
     own = LONG_CONTEXT - LONG_PREFIX
@@ -644,26 +871,32 @@ def run_longdecode(args, world, rank, local, peaks, peak_kind):
             handles.append(h)
         manager.release(root)                                 # the 16 sharers keep the pages
     inputs = [W.step_inputs(manager, handles, 1, 32, gen, lengths=[LONG_CONTEXT + s] * n_req)
-              for s in range(steps + args.warmup)]
+              for s in range(steps + warmup)]
     torch.cuda.synchronize()
+    setup_s = time.perf_counter() - t_setup
 
-    last = [None]
+    last = [None, None]
+    host_ms = [0.0]
 
     def step(s, ev=None):
+        t0 = time.perf_counter()
         batch = manager.begin_batch(handles, 1)
+        host_ms[0] += (time.perf_counter() - t0) * 1e3
         q, k, v = inputs[s]
         if ev is not None:
             ev[0].record()
         last[0] = batch.write_attend_layer(0, k, v, q)  # one launch: the decode kernel writes the rows
+        last[1] = (batch, k, v, q)
         if ev is not None:
             ev[1].record()
         manager.commit_batch(handles, 1)
 
-    for s in range(args.warmup):
+    for s in range(warmup):
         step(steps + s)
     torch.cuda.synchronize()
     for h in handles:  # undo the warm-up appends so the timed steps start at 32768
         manager.truncate(h, LONG_CONTEXT)
+    host_ms[0] = 0.0
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
@@ -674,9 +907,14 @@ def run_longdecode(args, world, rank, local, peaks, peak_kind):
             step(s, evs[s])
         end.record()
         torch.cuda.synchronize()
+        t_done = time.perf_counter()
         barrier(world)
+        waited_ms = (time.perf_counter() - t_done) * 1e3   # this rank idle at the barrier
+        b, k, v, q = last[1]
+        clocks.hold(lambda: b.write_attend_layer(0, k, v, q))  # the last step again (same rows)
     manager.check_device_errors()
-    ms = max_over_ranks(start.elapsed_time(end), world)
+    ms_local = start.elapsed_time(end)
+    ms = max_over_ranks(ms_local, world)
     attn_ms = sum(a.elapsed_time(b) for a, b in evs) / steps
     checksums = gather_over_ranks(float(last[0].double().sum().item()), world)
     row = 8 * 128 * 2 * 2  # K + V bytes per token
@@ -684,9 +922,17 @@ def run_longdecode(args, world, rank, local, peaks, peak_kind):
     logical_per_step = sum(n_req * (LONG_CONTEXT + s + 1) for s in range(steps)) * row / steps
     achieved = unique_per_step / (attn_ms / 1e3) / 1e9
     tokens = sum_over_ranks(float(n_req * steps), world)
+    per_rank = {
+        "elapsed_ms_per_step": [round(x / steps, 4) for x in gather_over_ranks(ms_local, world)],
+        "kernel_ms_per_step": [round(x, 4) for x in gather_over_ranks(attn_ms, world)],
+        "kernel_unique_GB_s": [round(x, 1) for x in gather_over_ranks(achieved, world)],
+        "begin_batch_host_ms_per_step": [round(x / steps, 4) for x in gather_over_ranks(host_ms[0], world)],
+        "barrier_wait_ms": [round(x, 3) for x in gather_over_ranks(waited_ms, world)],
+        "requests": [int(x) for x in gather_over_ranks(float(n_req), world)],
+    }
     return {
         "metric": "long-context decode tok/s (config 5)", "value": round(tokens / (ms / 1e3), 1),
-        "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
+        "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warmup,
         "ms_per_step": round(ms / steps, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded N(0,1), QK-norm + RoPE theta 1e6, shuffled pages",
@@ -701,6 +947,8 @@ def run_longdecode(args, world, rank, local, peaks, peak_kind):
                      "logical_GB_s": round(logical_per_step / (attn_ms / 1e3) / 1e9, 1), "traffic": None,
                      "kernel": "decode_attention_kernel"},
         "attention_ms_per_step": round(attn_ms, 4),
+        "per_rank": per_rank,
+        "setup_s_rank0": round(setup_s, 1),
         "gpu_launches": steps,
         "clocks": clocks.summary(),
         "output_checksums": [round(c, 6) for c in checksums],
@@ -866,20 +1114,63 @@ def run_engine(args, world, rank, impl: str, step: str = "reference"):
     }
 
 
+def engine_leg(args):
+    """Config 4 beside the headline (N=1): this repository's engine tick (packed prefill +
+    decode passes, decode-only ticks replayed from CUDA graphs) and hayate's own tick
+    (``Engine.generate``), both on this repository's KV manager and the same random-init
+    Qwen3-4B; output tok/s of each. Needs hayate's model and engine from baseline/_ref."""
+    import argparse as _ap
+
+    import torch
+
+    quick = _ap.Namespace(**{**vars(args), "warmup": 1})
+    try:
+        ours = run_engine(quick, 1, 0, "ours", step="graphs")
+        if "unavailable" in ours:
+            return ours
+        torch.cuda.empty_cache()
+        theirs = run_engine(quick, 1, 0, "ours", step="reference")
+    except Exception as exc:
+        return {"unavailable": f"{type(exc).__name__}: {str(exc).splitlines()[0][:200]}"}
+    return {"metric": ours["metric"], "value": ours["value"], "unit": "tok/s",
+            "total_tok_s": ours["total_tok_s"], "seconds": ours["seconds"], "config": ours["config"],
+            "hayate_tick": {k: theirs[k] for k in ("value", "total_tok_s", "seconds")},
+            "speedup_vs_hayate_tick": round(ours["value"] / theirs["value"], 3),
+            "what": "the same engine, model, requests and KV kernels; only the tick differs (hayate's "
+                    "Engine.generate runs one forward pass per distinct prompt-chunk length plus one "
+                    "for decode)"}
+
+
 # ---------------------------------------------------------------------------- reference arm
 def run_reference(args, world, rank):
-    """CPU oracle on the host cores, same metric/unit/config as the GPU arm (rank 0 only)."""
+    """The reference arm: hayate's own CPU attention path on the host cores (rank 0 only),
+    on this arm's metric and unit. Each step is a bounded sample of config 2 (its first 4
+    requests: begin_batch + write_layer + attend_layer, fp32); config 1 exactly is reported
+    beside it. Where the reference cannot be imported, the NumPy restatement stands in
+    (``kind`` "port", with the reason)."""
     if rank != 0:
         return None
+    threads = cpu_threads()
+    common = {"impl": "reference", "metric": "decode attn HBM GB/s (% of peak)", "unit": "GB/s",
+              "n_gpus": world, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+              "vs_baseline": None, "dtype": "f32",
+              "data": "synthetic N(0,1), QK-norm + RoPE theta 1e6 (the reference's rope.py), shuffled pages"}
+    ref = reference_cpu_path("config2_sample", steps=args.steps, warmup=args.warmup, budget_s=240.0)
+    if "unavailable" not in ref:
+        value = ref["value"]
+        cfg1 = reference_cpu_path("config1", steps=max(3, min(args.steps, 20)), warmup=1, budget_s=30.0)
+        return {**common, "value": value, "steps": ref["steps_timed"], "ms_per_step": ref["ms_per_step"],
+                "config": {"workload": ref["sample"],
+                           "query_heads": 32, "kv_heads": 8, "head_dim": 128, "page_size": 128},
+                "cpu_baseline": {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample", "path")},
+                "config1": cfg1,
+                "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    # fallback: the restatement on one config-2 request per step
     import oracle
     from threadpoolctl import threadpool_limits
 
-    threads = cpu_threads()
     ctx = decode_lengths(1000)
     rng = np.random.RandomState(7)
-    step_bytes_per_req = [n * 8 * 128 * 2 * 2 for n in ctx]
-    # each step: one request (rotating over the first 8 of the config-2 batch, whose pools
-    # are built once), K/V scatter + attention through the page table
     sample = list(range(8))
     pools = {}
     for r in sample:
@@ -901,21 +1192,16 @@ def run_reference(args, world, rank):
             dt = time.perf_counter() - t0
             if i >= args.warmup:
                 t_total += dt
-                b_total += step_bytes_per_req[r]
+                b_total += n * 8 * 128 * 2 * 2
     value = b_total / t_total / 1e9
-    return {
-        "impl": "reference",
-        "metric": "decode attn HBM GB/s (% of peak)", "value": round(value, 3), "unit": "GB/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(t_total / args.steps * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic N(0,1), config-2 lengths",
-        "config": {"workload": "config 2: paged decode sweep; each step = one request of the 64-request batch",
-                   "query_heads": 32, "kv_heads": 8, "head_dim": 128, "page_size": 128},
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": "one request per step, rotating over 8 requests of the config-2 batch"},
-        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
+    return {**common, "value": round(value, 3), "steps": args.steps,
+            "ms_per_step": round(t_total / args.steps * 1e3, 3),
+            "config": {"workload": "config 2: paged decode sweep; each step = one request of the 64-request batch",
+                       "query_heads": 32, "kv_heads": 8, "head_dim": 128, "page_size": 128},
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": "one request per step, rotating over 8 requests of the config-2 batch",
+                             "reason": "reference not importable: " + ref["unavailable"]},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 # ---------------------------------------------------------------------------- main
@@ -969,6 +1255,14 @@ def main():
             # heaviest in two)
             result["prefill_long_prefix"] = run_prefill(args, world, rank, local, peaks, peak_kind,
                                                         steps=20, warmup=3, prefix_max=32768)
+            # config 5 at every N: the request-partitioned long-context decode the 1/2/4/8-GPU
+            # tok/s is quoted on (its own 128 steps, whatever --steps says)
+            torch.cuda.empty_cache()
+            result["longdecode"] = run_longdecode(args, world, rank, local, peaks, peak_kind,
+                                                  steps=LONG_STEPS, warmup=3)
+            if world == 1 and not args.no_engine:
+                torch.cuda.empty_cache()
+                result["engine"] = engine_leg(args)
     elif args.workload == "prefill":
         result = run_prefill(args, world, rank, local, peaks, peak_kind)
     else:

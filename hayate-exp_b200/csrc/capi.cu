@@ -1228,4 +1228,15 @@ int hyt_wait_self_test(int32_t* error_word, int64_t* elapsed_ns, void* stream) {
   return HYT_OK;
 }
 
+int hyt_read_probe(const void* src, size_t bytes, uint32_t* sink, int32_t ctas, void* stream) {
+  g_last_error.clear();
+  if (src == nullptr || sink == nullptr) return fail(HYT_ERR_INVALID, "null src or sink");
+  if (bytes == 0 || bytes % 16 || reinterpret_cast<uintptr_t>(src) % 16)
+    return fail(HYT_ERR_INVALID, "src must be 16-byte aligned and bytes a positive multiple of 16");
+  if (ctas < 1 || ctas > 65535) return fail(HYT_ERR_INVALID, "ctas must be in [1, 65535]");
+  cudaError_t err = hyt::run_read_probe(src, bytes, sink, ctas, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "read probe launch");
+  return HYT_OK;
+}
+
 }  // extern "C"

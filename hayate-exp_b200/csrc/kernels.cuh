@@ -179,5 +179,6 @@ cudaError_t run_norm_rope_scatter(const NormRopeParams& p, int dtype, cudaStream
 
 // Runs the bounded mbarrier wait into its time limit (see self_test.cu).
 cudaError_t run_wait_self_test(int32_t* error_word, int64_t* elapsed_ns, cudaStream_t stream);
+cudaError_t run_read_probe(const void* src, size_t bytes, uint32_t* sink, int ctas, cudaStream_t stream);
 
 }  // namespace hyt

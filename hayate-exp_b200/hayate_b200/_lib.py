@@ -82,6 +82,7 @@ SIGNATURES = {
     "hyt_attention_workspace_bytes": (_c_size, [_c_i32] * 8),
     "hyt_workspace_init": (ctypes.c_int, [_c_p, _c_size, _c_p]),
     "hyt_wait_self_test": (ctypes.c_int, [_c_p, _c_p, _c_p]),
+    "hyt_read_probe": (ctypes.c_int, [_c_p, _c_size, _c_p, _c_i32, _c_p]),
 }
 
 _lock = threading.Lock()

@@ -404,6 +404,19 @@ def wait_self_test(error_word: torch.Tensor) -> tuple[int, int]:
     return first, second
 
 
+def read_probe(buf: torch.Tensor, sink: torch.Tensor) -> None:
+    """Launch the plain streaming-read kernel (``hyt_read_probe``) over ``buf``'s bytes on the
+    current stream: the HBM read ceiling the decode kernel is compared with (measurement only).
+    ``sink`` is a CUDA int32 tensor with one element per CTA (its length sets the grid)."""
+    _require_cuda(buf)
+    _require_cuda(sink)
+    if sink.dtype != torch.int32 or not sink.is_contiguous() or not buf.is_contiguous():
+        raise ValueError("buf must be contiguous and sink a contiguous int32 tensor")
+    nbytes = buf.numel() * buf.element_size()
+    rc = _lib.lib().hyt_read_probe(buf.data_ptr(), nbytes, sink.data_ptr(), sink.numel(), _stream_ptr())
+    _lib.check(rc, "hyt_read_probe")
+
+
 # ---------------------------------------------------------------------------- prefill schedule
 def prefill_plan(cache_lens, query_len: int, num_q_heads: int, num_sms: int, max_splits: int = 128,
                  q_lens=None, item_overhead: float = 0.0, merge_cost: float = 0.0):

@@ -331,6 +331,12 @@ int hyt_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
  * in flight when the kernel exits, so the context stays usable. Takes about 1 s. */
 int hyt_wait_self_test(int32_t* error_word, int64_t* elapsed_ns, void* stream);
 
+/* Measurement only (no hayate counterpart): a plain streaming read of `bytes` (a positive
+ * multiple of 16, src 16-byte aligned) by `ctas` CTAs of 512 threads, 16-byte loads, four
+ * in flight per thread; writes one XOR word per CTA to sink (device, uint32[ctas]). Timed
+ * around, it gives the HBM read ceiling the memory-bound decode kernel is compared with. */
+int hyt_read_probe(const void* src, size_t bytes, uint32_t* sink, int32_t ctas, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

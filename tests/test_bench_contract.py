@@ -1,5 +1,6 @@
 """bench.py's reference arm runs on the host cores and prints the driver's JSON line
-(CPU only: the oracle port on a bounded sample)."""
+(CPU only): hayate's own CPU attention path from baseline/_ref on a bounded sample of
+config 2, with config 1 beside it, or the NumPy restatement where the reference is absent."""
 
 from __future__ import annotations
 
@@ -22,7 +23,12 @@ def test_reference_arm_prints_the_contract_line():
         assert key in line, key
     assert line["metric"] == "decode attn HBM GB/s (% of peak)" and line["unit"] == "GB/s"
     assert line["value"] > 0 and line["steps"] == 1
-    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    installed = os.path.isdir(os.path.join(ROOT, "baseline", "_ref", "hayate"))
+    assert line["cpu_baseline"]["kind"] == ("reference" if installed else "port")
+    assert line["cpu_baseline"]["cores"] >= 1
+    if installed:
+        assert line["config1"]["kind"] == "reference" and line["config1"]["value"] > 0
+        assert "config 1" in line["config1"]["sample"]
     assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
 
