@@ -842,8 +842,9 @@ def run_longdecode(args, world, rank, local, peaks, peak_kind, steps=None, warmu
 
     Besides tok/s (whole job, max over ranks) the leg reports, per rank and gathered in rank
     order, what bounds the 1 -> N curve: the rank's decode-kernel time per step and its GB/s
-    of unique bytes, the host time of ``begin_batch`` per step, the rank's own elapsed time
-    and how long it waited at the closing barrier for the slowest rank."""
+    of unique bytes, the host time of ``begin_batch`` (alone, and inside the loop where it
+    also blocks on the upload ring once the host is 4 steps ahead), the rank's own elapsed
+    time and how long it waited at the closing barrier for the slowest rank."""
     import torch
 
     from hayate_b200 import PagedKVCacheManager
@@ -913,6 +914,13 @@ def run_longdecode(args, world, rank, local, peaks, peak_kind, steps=None, warmu
         b, k, v, q = last[1]
         clocks.hold(lambda: b.write_attend_layer(0, k, v, q))  # the last step again (same rows)
     manager.check_device_errors()
+    # begin_batch's own host time, with the GPU idle (inside the timed loop it also blocks
+    # on the upload ring whenever the host runs 4 steps ahead of the GPU)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(10):
+        manager.begin_batch(handles, 1)
+    host_only_ms = (time.perf_counter() - t0) * 1e3 / 10
     ms_local = start.elapsed_time(end)
     ms = max_over_ranks(ms_local, world)
     attn_ms = sum(a.elapsed_time(b) for a, b in evs) / steps
@@ -926,7 +934,8 @@ def run_longdecode(args, world, rank, local, peaks, peak_kind, steps=None, warmu
         "elapsed_ms_per_step": [round(x / steps, 4) for x in gather_over_ranks(ms_local, world)],
         "kernel_ms_per_step": [round(x, 4) for x in gather_over_ranks(attn_ms, world)],
         "kernel_unique_GB_s": [round(x, 1) for x in gather_over_ranks(achieved, world)],
-        "begin_batch_host_ms_per_step": [round(x / steps, 4) for x in gather_over_ranks(host_ms[0], world)],
+        "begin_batch_host_ms": [round(x, 4) for x in gather_over_ranks(host_only_ms, world)],
+        "begin_batch_in_loop_ms_per_step": [round(x / steps, 4) for x in gather_over_ranks(host_ms[0], world)],
         "barrier_wait_ms": [round(x, 3) for x in gather_over_ranks(waited_ms, world)],
         "requests": [int(x) for x in gather_over_ranks(float(n_req), world)],
     }

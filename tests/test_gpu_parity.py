@@ -198,6 +198,64 @@ def test_kernels_flag_bad_page_ids_without_touching_memory():
         assert int(err.item()) & 1, kernel
 
 
+AUTO_SPLIT_CASES = [
+    ([10, 20], 8192),            # a grid sized for 8192 keys: most splits have nothing to do
+    ([30000], 0),                # one request: many splits per (request, head)
+    ([0, 1, 63, 64, 127, 128, 1000, 2431], 0),   # empty history, page edges
+    ([4096] * 3 + [5, 9000, 77], 16384),         # long and short requests, slack in max_kv_len
+]
+
+
+@pytest.mark.parametrize("lengths, max_kv", AUTO_SPLIT_CASES, ids=str)
+def test_auto_split_decode_matches_oracle(lengths, max_kv):
+    """The decode step with the library's own split size (split_tokens 0), the fused row write
+    and a max_kv_len larger than needed: every request against the oracle, twice (the split
+    counters are left zero), on shapes that leave splits idle, cut one request into many
+    splits, or mix empty, short and long requests."""
+    manager, _, batch, q, k, v = build_step(lengths, 1, seed=len(lengths) + 3)
+    max_kv = max(max_kv, batch.max_kv_len)
+    need = ops.attention_workspace_bytes(len(lengths), 1, 32, 8, 128, max_kv, q.dtype, 0)
+    ws = ops.new_workspace(need, "cuda")
+    outs = []
+    for _ in range(2):  # a second call: the unit counters were left zero
+        outs.append(ops.paged_attention_scatter(q, k, v, manager.k_cache, manager.v_cache, 0,
+                                                batch.page_table, batch.cache_lens_i32, 128, max_kv,
+                                                workspace=ws, error_word=manager.error_word))
+    torch.cuda.synchronize()
+    manager.check_device_errors()
+    assert torch.equal(outs[0], outs[1])
+    if need:  # the split counters sit at the workspace's start and are left zero
+        assert int(ws[: len(lengths) * 8 * 4].view(torch.int32).abs().sum()) == 0
+    got = outs[0].float().cpu().numpy()
+    ref = oracle_request_rows(manager, batch, q, range(len(lengths)))
+    err = max(float(np.abs(got[b] - ref[b]).max()) for b in range(len(lengths)))
+    assert err <= 2e-2, err
+
+
+def test_auto_split_decode_flags_a_bad_page_and_recovers():
+    """A page id outside the pool in the middle of a long request: the decode kernel flags
+    it, the split that holds it loads nothing, the counters are left zero and the next clean
+    call matches the oracle."""
+    manager, _, batch, q, k, v = build_step([9000, 300], 1, seed=6)
+    batch.write_layer(0, k, v)
+    table = batch.page_table.clone()
+    table[0, 30] = manager.num_pages + 3
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ws = ops.new_workspace(ops.attention_workspace_bytes(2, 1, 32, 8, 128, batch.max_kv_len, q.dtype, 0), "cuda")
+    ops.paged_attention(q, manager.k_cache, manager.v_cache, 0, table, batch.cache_lens_i32, 128,
+                        batch.max_kv_len, workspace=ws, error_word=err)
+    torch.cuda.synchronize()
+    assert ops.read_device_errors(err) == ["page id outside the pool"]
+    assert int(ws[:64].view(torch.int32).abs().sum()) == 0  # counters still left zero
+    good = ops.paged_attention(q, manager.k_cache, manager.v_cache, 0, batch.page_table,
+                               batch.cache_lens_i32, 128, batch.max_kv_len, workspace=ws,
+                               error_word=manager.error_word)
+    torch.cuda.synchronize()
+    manager.check_device_errors()
+    ref = oracle_request_rows(manager, batch, q, [0, 1])
+    assert max(float(np.abs(good.float().cpu().numpy()[b] - ref[b]).max()) for b in (0, 1)) <= 2e-2
+
+
 def test_attend_output_layout_is_transpose_friendly():
     manager, _, batch, q, k, v = build_step([10, 20], 1, seed=1)
     batch.write_layer(0, k, v)

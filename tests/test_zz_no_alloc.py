@@ -96,6 +96,17 @@ def test_noalloc_decode_matches_workspace_decode_on_two_calls():
     assert err <= TOL, err
 
 
+def test_noalloc_library_split_matches_workspace_decode():
+    """split_tokens 0: the library's own split size for this batch, on both entry points."""
+    manager, batch, q = _decode_step(LENGTHS, seed=19)
+    expected = _with_workspace(manager, batch, q, 0)
+    for _ in range(2):
+        got = _noalloc(manager, batch, q, 0)
+        torch.cuda.synchronize()
+        assert torch.equal(got, expected)
+    manager.check_device_errors()
+
+
 def test_noalloc_many_splits_then_few():
     """A call with many splits fills much of the array; a later call with fewer splits lays
     its partials out differently over the same bytes and must not read the old ones."""
