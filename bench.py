@@ -97,9 +97,9 @@ def decode_lengths(seed: int, batch: int = 64, lo: int = 1024, hi: int = 8192):
 
 
 # DRAM bytes per launch of the dominant kernel (dram__bytes_read.sum + dram__bytes_write.sum)
-# from one ncu capture each: config 2 decode scaled from a 16-request capture by kv tokens
-# (1.028 x the algorithmic bytes), config 3 prefill captured at full size.
-DECODE_CFG2_TRAFFIC = 1.217e9
+# from one ncu capture each at full size: config 2's fused decode launch (1.1938 GB read +
+# 7.37 MB written, 1.013 x the algorithmic bytes) and config 3's prefill launch.
+DECODE_CFG2_TRAFFIC = 1.2012e9
 PREFILL_CFG3_TRAFFIC = 145.36e6
 
 
