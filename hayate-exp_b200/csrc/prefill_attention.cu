@@ -134,7 +134,7 @@ __device__ __forceinline__ float exp_tile(const float (&s)[64], uint64_t scale2,
 }
 
 struct Barriers {
-  uint64_t q_full;
+  uint64_t q_full[2];  // Q_A, Q_B
   uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
   uint64_t s_full[2], p_full[2];  // per tile (A, B)
   uint64_t o_done, drain;
@@ -164,16 +164,17 @@ __device__ __forceinline__ void merge_split(const PrefillPlan& plan, int slot, c
     const bool use0 = a.y > 0.f, use1 = c.y > 0.f;
     const float m = use0 && use1 ? fmaxf(a.x, c.x) : (use0 ? a.x : (use1 ? c.x : 0.f));
     const float f0 = use0 ? ex2(a.x - m) : 0.f, f1 = use1 ? ex2(c.x - m) : 0.f;
-    const float l = a.y * f0 + c.y * f1;
+    const float l = __fadd_rn(__fmul_rn(a.y, f0), __fmul_rn(c.y, f1));  // as the in-kernel merge
     const float inv = l > 0.f ? 1.f / l : 0.f;
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (use0) {
+    if (use0) {  // part 0's term rounded, part 1's fused into it (the in-kernel merge's order)
       const float4 v = __ldcg(&wo[(u0 * 32 + c4) * kRows + r]);
-      o = make_float4(v.x * f0, v.y * f0, v.z * f0, v.w * f0);
+      o = make_float4(__fmul_rn(v.x, f0), __fmul_rn(v.y, f0), __fmul_rn(v.z, f0), __fmul_rn(v.w, f0));
     }
     if (use1) {
       const float4 v = __ldcg(&wo[(u1 * 32 + c4) * kRows + r]);
-      o = make_float4(o.x + v.x * f1, o.y + v.y * f1, o.z + v.z * f1, o.w + v.w * f1);
+      o = make_float4(__fmaf_rn(v.x, f1, o.x), __fmaf_rn(v.y, f1, o.y), __fmaf_rn(v.z, f1, o.z),
+                      __fmaf_rn(v.w, f1, o.w));
     }
     uint2 w;
     w.x = Elem<T>::pack2(o.x * inv, o.y * inv);
@@ -321,10 +322,57 @@ __global__ void __maxnreg__(96)
     return;
   }
 
-  if (threadIdx.x == 0) {
+  int32_t* err = p.error_word;
+  volatile int* abort = &bars->abort;
+  const int plane = p.layer * p.num_kv_heads + g;
+  // producer state, shared by its start-up loads (issued before the CTA-wide barrier) and
+  // its loop; an earlier CTA's wait gave up: load nothing (the CTA writes zeros)
+  int bad = 0;
+  // pool row of key tile j, or -1 (and the error bit in `why`) for a page id outside the
+  // pool; the table row is long enough for every tile (checked above)
+  auto tile_row = [&](int j, int& why) {
+    const int tok = j * kKeys;
+    const int32_t page = table[tok >> p.page_shift];
+    if (page < 0 || page >= p.num_pages) {
+      why |= HYT_DEVERR_PAGE_RANGE;
+      return -1;
+    }
+    return (page << p.page_shift) + (tok & page_mask);
+  };
+  // K and V of ring position j (key tile k_lo + j) into stage j & 1: a TMA load, or, once a
+  // page id was refused, a plain arrival so every role still walks the same tiles
+  auto load_tile = [&](int j) {
+    const int st = j & 1;
+    const uint32_t ph = (j >> 1) & 1;
+    const int row = bad ? -1 : tile_row(k_lo + j, bad);
+    if (j >= 2) mbar_wait(&bars->k_empty[st], ph ^ 1, err, abort);
+    uint8_t* kdst = smem + kKOff + st * kTileBytes;
+    if (!bad) {
+      mbar_arrive_expect_tx(&bars->k_full[st], kTileBytes);
+      tma_load_3d(kdst, &k_map, &bars->k_full[st], 0, row, plane);
+      tma_load_3d(kdst + kChunkBytes, &k_map, &bars->k_full[st], 64, row, plane);
+    } else {
+      mbar_arrive(&bars->k_full[st]);
+    }
+    if (j >= 2) mbar_wait(&bars->v_empty[st], ph ^ 1, err, abort);
+    uint8_t* vdst = smem + kVOff + st * kTileBytes;
+    if (!bad) {
+      mbar_arrive_expect_tx(&bars->v_full[st], kTileBytes);
+      tma_load_3d(vdst, &v_map, &bars->v_full[st], 0, row, plane);
+      tma_load_3d(vdst + kChunkBytes, &v_map, &bars->v_full[st], 64, row, plane);
+    } else {
+      mbar_arrive(&bars->v_full[st]);
+    }
+  };
+  const int n_early = min(n_loop, 2);  // ring positions the producer loads before the barrier
+
+  if (warp == kProducerWarp && lane == 0) {
+    // Start-up: the producer initialises the barriers and issues Q_A, Q_B and the first
+    // two K/V tiles at once, while warp 0 allocates tensor memory; the CTA-wide barrier
+    // below then publishes the barriers to every other thread.
     bars->abort = 0;
     bars->bad = 0;
-    mbar_init(&bars->q_full, P.q_tma ? 1 : kSoftmaxThreads);
+    for (int x = 0; x < 2; ++x) mbar_init(&bars->q_full[x], P.q_tma ? 1 : kSoftmaxThreads);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->k_empty[s], 1);
@@ -337,6 +385,28 @@ __global__ void __maxnreg__(96)
     mbar_init(&bars->drain, 1);
     mbar_init(&bars->prod_done, 1);
     fence_barrier_init();
+    fence_proxy_async_smem();  // the initialised barriers, before this thread's TMA uses them
+    bad = (err != nullptr && (*reinterpret_cast<volatile int32_t*>(err) & HYT_DEVERR_WAIT_TIMEOUT))
+              ? HYT_DEVERR_WAIT_TIMEOUT : 0;
+    if (P.q_tma) {  // Q first: QK_x waits for Q_x and K tile 0
+      const int q_row0 = kPacked ? p.q_start[b] + t0 : t0;
+      const int q_req = kPacked ? 0 : b;
+#pragma unroll
+      for (int qx = 0; qx < 2; ++qx) {
+        mbar_arrive_expect_tx(&bars->q_full[qx], kTileBytes);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint8_t* dst = smem + kQOff + qx * kTileBytes + c * kChunkBytes;
+          if (P.q_ht)
+            tma_load_4d(dst, &q_map, &bars->q_full[qx], c * 64, h0 + qx, q_row0, q_req);
+          else
+            tma_load_4d(dst, &q_map, &bars->q_full[qx], c * 64, q_row0, h0 + qx, q_req);
+        }
+      }
+    }
+    tma_prefetch_desc(&k_map);
+    tma_prefetch_desc(&v_map);
+    for (int j = 0; j < n_early; ++j) load_tile(j);
   }
   if (warp == 0) {
     tmem_alloc(&bars->tmem_base, kTmemCols);
@@ -347,44 +417,10 @@ __global__ void __maxnreg__(96)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
   const uint32_t smem_base = smem_u32(smem);
-  int32_t* err = p.error_word;
-  volatile int* abort = &bars->abort;
 
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      if (P.q_tma) {  // Q first: the first QK waits for it and for K tile 0
-        const int q_row0 = kPacked ? p.q_start[b] + t0 : t0;
-        const int q_req = kPacked ? 0 : b;
-        mbar_arrive_expect_tx(&bars->q_full, 2 * kTileBytes);
-#pragma unroll
-        for (int qx = 0; qx < 2; ++qx)
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            uint8_t* dst = smem + kQOff + qx * kTileBytes + c * kChunkBytes;
-            if (P.q_ht)
-              tma_load_4d(dst, &q_map, &bars->q_full, c * 64, h0 + qx, q_row0, q_req);
-            else
-              tma_load_4d(dst, &q_map, &bars->q_full, c * 64, q_row0, h0 + qx, q_req);
-          }
-      }
-      tma_prefetch_desc(&k_map);
-      tma_prefetch_desc(&v_map);
-      const int plane = p.layer * p.num_kv_heads + g;
-      // an earlier CTA's wait gave up: load nothing (the CTA writes zeros)
-      int bad = (err != nullptr && (*reinterpret_cast<volatile int32_t*>(err) & HYT_DEVERR_WAIT_TIMEOUT))
-                    ? HYT_DEVERR_WAIT_TIMEOUT : 0;
-      // pool row of key tile j, or -1 (and the error bit in `why`) for a page id outside
-      // the pool; the table row is long enough for every tile (checked above)
-      auto tile_row = [&](int j, int& why) {
-        const int tok = j * kKeys;
-        const int32_t page = table[tok >> p.page_shift];
-        if (page < 0 || page >= p.num_pages) {
-          why |= HYT_DEVERR_PAGE_RANGE;
-          return -1;
-        }
-        return (page << p.page_shift) + (tok & page_mask);
-      };
       auto prefetch = [&](int j) {  // K and V of tile j into L2
         int why = 0;
         const int row = tile_row(j, why);
@@ -394,34 +430,14 @@ __global__ void __maxnreg__(96)
         tma_prefetch_l2_3d(&v_map, 0, row, plane);
         tma_prefetch_l2_3d(&v_map, 64, row, plane);
       };
-      // Tiles 0 and 1 are loaded at once (both ring stages are free); from iteration 1 on,
-      // each iteration prefetches into L2 the tile kPrefetchTiles beyond the one it loads.
-      // No prefetch burst at start-up: the whole first wave loads Q and its first tiles
-      // then, sharing HBM. Once a page id is refused, later stages are released without a
-      // load (plain arrivals) so every role still walks the same number of tiles.
-      for (int j = 0; j < n_loop; ++j) {  // ring position j holds key tile k_lo + j
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!bad && j >= 1 && j + kPrefetchTiles < n_loop) prefetch(k_lo + j + kPrefetchTiles);
-        const int row = bad ? -1 : tile_row(k_lo + j, bad);
-        if (j >= 2) mbar_wait(&bars->k_empty[st], ph ^ 1, err, abort);
-        uint8_t* kdst = smem + kKOff + st * kTileBytes;
-        if (!bad) {
-          mbar_arrive_expect_tx(&bars->k_full[st], kTileBytes);
-          tma_load_3d(kdst, &k_map, &bars->k_full[st], 0, row, plane);
-          tma_load_3d(kdst + kChunkBytes, &k_map, &bars->k_full[st], 64, row, plane);
-        } else {
-          mbar_arrive(&bars->k_full[st]);
-        }
-        if (j >= 2) mbar_wait(&bars->v_empty[st], ph ^ 1, err, abort);
-        uint8_t* vdst = smem + kVOff + st * kTileBytes;
-        if (!bad) {
-          mbar_arrive_expect_tx(&bars->v_full[st], kTileBytes);
-          tma_load_3d(vdst, &v_map, &bars->v_full[st], 0, row, plane);
-          tma_load_3d(vdst + kChunkBytes, &v_map, &bars->v_full[st], 64, row, plane);
-        } else {
-          mbar_arrive(&bars->v_full[st]);
-        }
+      // Positions 0 and 1 were loaded at start-up (both ring stages are free); from
+      // iteration 1 on, each iteration prefetches into L2 the tile kPrefetchTiles beyond the
+      // one it loads. No prefetch burst at start-up: the whole first wave loads Q and its
+      // first tiles then, sharing HBM.
+      if (!bad && n_early > 1 && 1 + kPrefetchTiles < n_loop) prefetch(k_lo + 1 + kPrefetchTiles);
+      for (int j = n_early; j < n_loop; ++j) {  // ring position j holds key tile k_lo + j
+        if (!bad && j + kPrefetchTiles < n_loop) prefetch(k_lo + j + kPrefetchTiles);
+        load_tile(j);
       }
       if (bad) {
         flag_error(err, bad);
@@ -432,7 +448,10 @@ __global__ void __maxnreg__(96)
         mbar_drain(&bars->k_full[j & 1], (j >> 1) & 1);
         mbar_drain(&bars->v_full[j & 1], (j >> 1) & 1);
       }
-      if (P.q_tma) mbar_drain(&bars->q_full, 0);
+      if (P.q_tma) {
+        mbar_drain(&bars->q_full[0], 0);
+        mbar_drain(&bars->q_full[1], 0);
+      }
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
@@ -490,9 +509,10 @@ __global__ void __maxnreg__(96)
       }
       __syncwarp();
     };
-    mbar_wait(&bars->q_full, 0, err, abort);
+    mbar_wait(&bars->q_full[0], 0, err, abort);
     mbar_wait(&bars->k_full[0], 0, err, abort);
     issue(0, 0, false, true, nullptr, nullptr);
+    mbar_wait(&bars->q_full[1], 0, err, abort);
     issue(1, 0, false, true, &bars->k_empty[0], nullptr);
     for (int j = 0; j < n_loop; ++j) {
       const bool more = j + 1 < n_loop;
@@ -548,7 +568,8 @@ __global__ void __maxnreg__(96)
         *reinterpret_cast<uint4*>(smem + kQOff + qx * kTileBytes + sw128_offset(qr, c)) = v[i];
       }
       fence_proxy_async_smem();
-      mbar_arrive(&bars->q_full);
+      mbar_arrive(&bars->q_full[0]);
+      mbar_arrive(&bars->q_full[1]);
     }
 
     const float scale_log2 = p.scale * kLog2e;
@@ -670,7 +691,9 @@ __global__ void __maxnreg__(96)
         const float m = use_own && use_other ? fmaxf(m_run, other.x) : (use_own ? m_run : (use_other ? other.x : 0.f));
         own_scale = use_own ? ex2(m_run - m) : 0.f;
         partner_scale = use_other ? ex2(other.x - m) : 0.f;
-        const float lsum = own_l * own_scale + other.y * partner_scale;
+        // products rounded on their own and added (no fused multiply-add): the same sum
+        // whichever half arrived second
+        const float lsum = __fadd_rn(__fmul_rn(own_l, own_scale), __fmul_rn(other.y, partner_scale));
         inv = lsum > 0.f ? 1.f / lsum : 0.f;
         if (use_other) partner = reinterpret_cast<const float4*>(P.plan.ws_o) + unit * 32 * kRows;
         if (threadIdx.x == 0) *counter = 0;  // both halves are done with the slot
@@ -687,13 +710,19 @@ __global__ void __maxnreg__(96)
 #pragma unroll
       for (int i = 0; i < 32; ++i) f[i] = use_own ? __uint_as_float(o[i]) * own_scale : 0.f;
       if (partner != nullptr) {
+        // the two halves combine in one fixed order, part 0's term rounded, part 1's fused
+        // into it, so the rows do not depend on which half arrived second
+        const bool own_first = (split & 1) == 0;
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
           const float4 q4 = __ldcg(&partner[(half * 16 + c * 8 + v) * kRows + r]);
-          f[4 * v] += q4.x * partner_scale;
-          f[4 * v + 1] += q4.y * partner_scale;
-          f[4 * v + 2] += q4.z * partner_scale;
-          f[4 * v + 3] += q4.w * partner_scale;
+          const float pv[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float mine = use_own ? __uint_as_float(o[4 * v + e]) : 0.f;
+            f[4 * v + e] = own_first ? __fmaf_rn(pv[e], partner_scale, __fmul_rn(mine, own_scale))
+                                     : __fmaf_rn(mine, own_scale, __fmul_rn(pv[e], partner_scale));
+          }
         }
       }
 #pragma unroll
