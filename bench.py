@@ -23,7 +23,9 @@ max over ranks (NCCL all_reduce of the elapsed times only).
 The default run adds, beside the config-2 headline: config 3 (and the same shape
 on longer prefixes), config 5 at every N (its own 128 steps, with each rank's
 kernel time, host time and barrier wait), config 4's engine at N=1, the e2e
-number through the public API with host buffers, and the CPU baseline.
+number through the public API with host buffers, the CPU baseline, and at N=1
+the reference's own GPU attention (its torch.compile'd FlexAttention from
+baseline/_ref) timed on the same inputs beside configs 2 and 3.
 
 ``--impl reference`` times hayate's OWN CPU attention path (its unmodified
 ``PagedKVCacheManager``/``PagedKVBatch`` from ``baseline/_ref``, fp32, eager
@@ -73,11 +75,22 @@ def parse_args():
     ap.add_argument("--prefix-max", type=int, default=4096,
                     help="prefill workload: prefixes drawn from U[0, prefix-max] (config 3: 4096)")
     ap.add_argument("--reference-gpu", action="store_true",
-                    help="also time the reference's compiled FlexAttention path on the GPU (needs baseline/_ref)")
+                    help="time the reference's compiled FlexAttention path on the GPU at any N (by default "
+                         "only at N=1; needs baseline/_ref)")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip the reference's GPU path (timed beside ours by default at N=1)")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 128 if args.workload == "longdecode" else 2000
     return args
+
+
+def wants_reference_gpu(args, world: int, rank: int) -> bool:
+    """The reference's own GPU attention (its torch.compile'd FlexAttention) is timed beside
+    ours on rank 0 of a 1-GPU run unless --no-reference-gpu, or at any N with --reference-gpu."""
+    if rank != 0 or args.no_reference_gpu:
+        return False
+    return args.reference_gpu or world == 1
 
 
 def load_peaks():
@@ -439,7 +452,7 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
         "output_checksums": [round(c, 6) for c in checksums],
     }
     result["roofline"]["frac_of_read_ceiling"] = round(achieved / read_ceiling["GB_s"], 4)
-    if args.reference_gpu and rank == 0:
+    if wants_reference_gpu(args, world, rank):
         ref_gpu = reference_gpu_compare(manager, handles, q, k, v, out, kv_bytes / 1e9, "GB_s")
         if "ms" in ref_gpu:
             ref_gpu["ours_attention_ms"] = round(attn_ms, 4)
@@ -789,7 +802,7 @@ def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=N
         barrier(world)
         clocks.hold(step)
     manager.check_device_errors()
-    out = step()  # the rows (compared with the reference's when --reference-gpu)
+    out = step()  # the rows (compared with the reference's GPU path's)
     plan = batch.prefill_schedule(q)
     schedule = ("default grid" if plan is None else
                 f"planned: {plan[0].shape[0]} CTAs, {plan[1]} items cut in two (longest first)")
@@ -799,7 +812,7 @@ def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=N
     total_flops = sum_over_ranks(float(flops), world)
     achieved = flops / (attn_ms / 1e3) / 1e12
     ref_gpu = None
-    if args.reference_gpu and rank == 0:
+    if wants_reference_gpu(args, world, rank):
         ref_gpu = reference_gpu_compare(manager, handles, q, k, v, out, flops / 1e12, "TFLOP_s")
         if "ms" in ref_gpu:
             ref_gpu["ours_attention_ms"] = round(attn_ms, 4)
@@ -981,6 +994,10 @@ def reference_gpu_compare(manager, handles, q, k, v, ours_out, per_step_units, u
         import hayate.engine.paged_cache as ref
         from hayate.model.cache import Cache
 
+        # compile afresh for this shape: with dynamic=True a kernel compiled for an earlier
+        # comparison's shape (decode, T=1) would otherwise be reused for a prefill chunk
+        torch._dynamo.reset()
+        torch.cuda.empty_cache()
         T = q.shape[2]
         rm = ref.PagedKVCacheManager(1, manager.num_kv_heads, manager.head_dim, manager.capacity_tokens,
                                      manager.page_size, len(handles), torch.bfloat16, "cuda")
