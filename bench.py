@@ -378,16 +378,28 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
         barrier(world)
         torch.cuda.synchronize()
         start.record()
+        t_host = time.perf_counter()
         for i in range(args.steps):
             step(kern[i])
         end.record()
+        host_ms = (time.perf_counter() - t_host) * 1e3
         torch.cuda.synchronize()
         barrier(world)
         clocks.hold(step)
     ms_local = start.elapsed_time(end)
     kernel_ms = sum(a.elapsed_time(b) for a, b in kern) / args.steps
+    # the device idle inside the timed region: before the first launch, and between launches
+    first_gap = start.elapsed_time(kern[0][0])
+    between = sum(kern[i][1].elapsed_time(kern[i + 1][0]) for i in range(args.steps - 1))
     manager.check_device_errors()
     checksums = gather_over_ranks(float(out.double().sum().item()), world)
+    per_rank = {
+        "elapsed_ms_per_step": [round(x / args.steps, 4) for x in gather_over_ranks(ms_local, world)],
+        "kernel_ms": [round(x, 4) for x in gather_over_ranks(kernel_ms, world)],
+        "gap_before_first_launch_ms": [round(x, 4) for x in gather_over_ranks(first_gap, world)],
+        "gaps_between_launches_ms": [round(x, 4) for x in gather_over_ranks(between, world)],
+        "host_enqueue_ms_per_step": [round(x / args.steps, 4) for x in gather_over_ranks(host_ms, world)],
+    }
     ms_total = max_over_ranks(ms_local, world)
     total_bytes = sum_over_ranks(float(step_bytes), world)
     value = total_bytes * args.steps / (ms_total / 1e3) / 1e9
@@ -447,6 +459,7 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
                      "bytes_per_launch": step_bytes,
                      "kernel": "decode_attention_kernel (split-KV decode with the fused row scatter)"},
         "read_ceiling": read_ceiling,
+        "per_rank": per_rank,
         "gpu_launches": args.steps,
         "clocks": clocks.summary(),
         "output_checksums": [round(c, 6) for c in checksums],
