@@ -18,7 +18,10 @@ the reference's under ``--impl reference``).
 
 Multi-GPU: one process per GPU (torchrun), each rank owns its own pool and
 requests; there is no collective on the data path. Timing is by CUDA events,
-max over ranks (NCCL all_reduce of the elapsed times only).
+max over ranks (NCCL all_reduce of the elapsed times only). The headline's K
+timed steps are replayed from one CUDA graph captured from the same calls (no
+host launch inside the timed region); the same K steps launched one by one are
+timed beside it (`eager`), with per-launch events for the roofline.
 
 The default run adds, beside the config-2 headline: config 3 (and the same shape
 on longer prefixes), config 5 at every N (its own 128 steps, with each rank's
@@ -371,39 +374,64 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
     torch.cuda.synchronize()
     manager.check_device_errors()
 
+    # The timed region replays the K steps from one CUDA graph captured from the same calls
+    # (what a serving loop does with its decode steps): no host launch inside it, so eight
+    # ranks sharing one host's cores cannot leave their GPUs idle between steps. The same K
+    # steps launched one by one from Python run right before it: their per-launch events
+    # give the kernel time the roofline uses, and the device idle time between launches.
+    graph, graph_note = capture_steps(step, args.steps)
     kern = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             for _ in range(args.steps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         barrier(world)
         torch.cuda.synchronize()
-        start.record()
+        e0.record()
         t_host = time.perf_counter()
         for i in range(args.steps):
             step(kern[i])
-        end.record()
+        e1.record()
         host_ms = (time.perf_counter() - t_host) * 1e3
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record()
+        if graph is not None:
+            graph.replay()
+        else:
+            for i in range(args.steps):
+                step()
+        end.record()
         torch.cuda.synchronize()
         barrier(world)
         clocks.hold(step)
     ms_local = start.elapsed_time(end)
+    eager_local = e0.elapsed_time(e1)
     kernel_ms = sum(a.elapsed_time(b) for a, b in kern) / args.steps
-    # the device idle inside the timed region: before the first launch, and between launches
-    first_gap = start.elapsed_time(kern[0][0])
+    # device idle inside the eager loop: before the first launch, and between launches
+    first_gap = e0.elapsed_time(kern[0][0])
     between = sum(kern[i][1].elapsed_time(kern[i + 1][0]) for i in range(args.steps - 1))
     manager.check_device_errors()
     checksums = gather_over_ranks(float(out.double().sum().item()), world)
     per_rank = {
         "elapsed_ms_per_step": [round(x / args.steps, 4) for x in gather_over_ranks(ms_local, world)],
+        "eager_elapsed_ms_per_step": [round(x / args.steps, 4) for x in gather_over_ranks(eager_local, world)],
         "kernel_ms": [round(x, 4) for x in gather_over_ranks(kernel_ms, world)],
-        "gap_before_first_launch_ms": [round(x, 4) for x in gather_over_ranks(first_gap, world)],
-        "gaps_between_launches_ms": [round(x, 4) for x in gather_over_ranks(between, world)],
-        "host_enqueue_ms_per_step": [round(x / args.steps, 4) for x in gather_over_ranks(host_ms, world)],
+        "eager_gap_before_first_launch_ms": [round(x, 4) for x in gather_over_ranks(first_gap, world)],
+        "eager_gaps_between_launches_ms": [round(x, 4) for x in gather_over_ranks(between, world)],
+        "eager_host_enqueue_ms_per_step": [round(x / args.steps, 4) for x in gather_over_ranks(host_ms, world)],
     }
     ms_total = max_over_ranks(ms_local, world)
+    eager_total = max_over_ranks(eager_local, world)
     total_bytes = sum_over_ranks(float(step_bytes), world)
     value = total_bytes * args.steps / (ms_total / 1e3) / 1e9
-    achieved = step_bytes / (kernel_ms / 1e3) / 1e9
+    del graph
+    # the roofline's launch duration: the timed region holds only the K launches of the decode
+    # kernel, so its length / K is their average (back to back, as in a graph-replayed serving
+    # step); with the eager fallback, the per-launch events
+    launch_ms = ms_local / args.steps if graph_note.startswith(f"{args.steps} steps replayed") else kernel_ms
+    achieved = step_bytes / (launch_ms / 1e3) / 1e9
     peak = peaks["hbm_gbs"]
 
     # the two-launch step beside it (outside the timed region): scatter, then attention alone
@@ -457,8 +485,17 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
                      "traffic": DECODE_CFG2_TRAFFIC if len(ctx) == 64 else None,
                      "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + write.sum)",
                      "bytes_per_launch": step_bytes,
+                     "launch_ms": round(launch_ms, 4),
+                     "eager_launch_ms": round(kernel_ms, 4),
+                     "launch_timing": "timed-region length / K launches (graph-replayed, back to back); "
+                                      "eager_launch_ms: events around each launch of the eager loop, which "
+                                      "add the launch latency",
                      "kernel": "decode_attention_kernel (split-KV decode with the fused row scatter)"},
         "read_ceiling": read_ceiling,
+        "timing": graph_note,
+        "eager": {"value": round(total_bytes * args.steps / (eager_total / 1e3) / 1e9, 1),
+                  "ms_per_step": round(eager_total / args.steps, 4),
+                  "what": "the same K steps launched one by one from Python (max over ranks)"},
         "per_rank": per_rank,
         "gpu_launches": args.steps,
         "clocks": clocks.summary(),
@@ -476,6 +513,22 @@ def run_decode(args, world, rank, local, peaks, peak_kind):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline_decode(manager, batch, q, ctx)
     return result
+
+
+def capture_steps(step, n: int):
+    """The n steps captured into one CUDA graph (replayed as the timed region), or None and
+    the reason when capture is not possible (the eager loop is timed instead)."""
+    import torch
+
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(n):
+                step()
+        torch.cuda.synchronize()
+        return graph, f"{n} steps replayed from one CUDA graph captured from the same calls; CUDA events around the replay"
+    except Exception as exc:  # pragma: no cover - depends on the box
+        return None, f"eager loop ({type(exc).__name__} in graph capture: {str(exc).splitlines()[0][:120]})"
 
 
 def plain_read_ceiling(nbytes: int, world: int, repeats: int = 20):
