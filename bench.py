@@ -73,6 +73,9 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="headline workload only")
     ap.add_argument("--no-engine", action="store_true", help="skip the config-4 engine leg of the default run")
+    ap.add_argument("--long-groups", type=int, default=32,
+                    help="config 5: prefix groups of 16 requests in the job (32 = config 5; 4 = one "
+                         "rank's share at 8 GPUs)")
     ap.add_argument("--no-prefill-plan", action="store_true",
                     help="prefill on the default grid instead of the planned schedule")
     ap.add_argument("--prefix-max", type=int, default=4096,
@@ -909,10 +912,11 @@ def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=N
 LONG_GROUPS, LONG_PER_GROUP, LONG_PREFIX, LONG_CONTEXT, LONG_STEPS = 32, 16, 4096, 32768, 128
 
 
-def long_groups(rank: int, world: int) -> list[int]:
+def long_groups(rank: int, world: int, groups: int = LONG_GROUPS) -> list[int]:
     """Prefix groups of config 5 this rank serves: whole groups, round robin, so every
-    shared prefix stays on one GPU and no data crosses between ranks."""
-    return [g for g in range(LONG_GROUPS) if g % world == rank]
+    shared prefix stays on one GPU and no data crosses between ranks. ``groups`` < 32 runs
+    a share of config 5 (e.g. 4 groups: one rank's share at N=8) on fewer GPUs."""
+    return [g for g in range(groups) if g % world == rank]
 
 
 def run_longdecode(args, world, rank, local, peaks, peak_kind, steps=None, warmup=None):
@@ -932,7 +936,7 @@ def run_longdecode(args, world, rank, local, peaks, peak_kind, steps=None, warmu
     steps = args.steps if steps is None else steps
     warmup = args.warmup if warmup is None else warmup
     t_setup = time.perf_counter()
-    groups = long_groups(rank, world)
+    groups = long_groups(rank, world, args.long_groups)
     n_req = len(groups) * LONG_PER_GROUP
     own = LONG_CONTEXT - LONG_PREFIX
     unique = len(groups) * (LONG_PREFIX + LONG_PER_GROUP * own)
@@ -1024,7 +1028,10 @@ def run_longdecode(args, world, rank, local, peaks, peak_kind, steps=None, warmu
         "ms_per_step": round(ms / steps, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded N(0,1), QK-norm + RoPE theta 1e6, shuffled pages",
-        "config": {"workload": "config 5: 512 requests x 32768 context, groups of 16 share a 4096-token prefix, 1 layer",
+        "config": {"workload": ("config 5: 512 requests x 32768 context, groups of 16 share a 4096-token prefix, 1 layer"
+                                if args.long_groups == LONG_GROUPS else
+                                f"config 5's shapes, {args.long_groups} of its 32 prefix groups "
+                                f"({args.long_groups * LONG_PER_GROUP} requests)"),
                    "requests_this_rank": n_req, "groups_this_rank": len(groups),
                    "parallelism": f"request-parallel by prefix group x{world}",
                    "l2": "KV read per step tens of GB >> 126 MB L2"},

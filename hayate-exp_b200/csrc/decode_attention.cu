@@ -5,7 +5,8 @@
 // 0 .. cache_lens[b] + t (paged_cache.py:266-271), query head h reads KV head
 // h / group (FlexAttention enable_gqa), softmax scale 1/sqrt(128) by default.
 //
-// Work unit: one CTA per (split of up to split_tokens keys, KV head g, request b).
+// Work unit: one CTA per (split of up to split_tokens keys, KV head g, request b); a
+// request's keys are cut into equal 64-token-aligned pieces, no short last piece.
 // All group * query_len (<= 16) query rows that share KV head g ride in one
 // 16-row mma tile, so every K/V byte is read from HBM exactly once per step.
 //
@@ -83,10 +84,14 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   const int cache_len = p.cache_lens[b];
   const int kv_len = cache_len + p.query_len;
-  const int tok_begin = split * P.d.split_tokens;
-  if (tok_begin >= kv_len) return;  // uniform per CTA, before any barrier
-  const int tok_end = min(kv_len, tok_begin + P.d.split_tokens);
+  // this request's keys in nsplits pieces of equal size (a multiple of the 64-token tile,
+  // at most split_tokens): no short last piece. (nsplits - 1) * piece < kv_len, so every
+  // one of the nsplits pieces holds keys and the last-arriver count stays nsplits.
   int nsplits = (kv_len + P.d.split_tokens - 1) / P.d.split_tokens;
+  const int piece = nsplits > 0 ? ((kv_len + nsplits - 1) / nsplits + kTile - 1) / kTile * kTile : P.d.split_tokens;
+  const int tok_begin = split * piece;
+  if (tok_begin >= kv_len) return;  // uniform per CTA, before any barrier
+  const int tok_end = min(kv_len, tok_begin + piece);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
