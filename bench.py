@@ -718,17 +718,30 @@ def reference_cpu_path(which: str, steps: int, warmup: int, budget_s: float | No
     One step is one layer's write + attention for the whole sample. ``value`` is GB/s of the
     K/V rows attended, counted in fp32 (4 bytes per element, the dtype the reference runs
     in). Timing stops early once ``budget_s`` seconds of steps are done."""
-    import random
-
-    import torch
-
     mods, why = import_reference()
     if mods is None:
         return {"unavailable": why}
     paged_cache, Cache, compute_rope_params, apply_rope = mods
     from torch.nn.attention.flex_attention import flex_attention
 
+    # the swap lasts for this call only: the GPU comparisons later in the same process time
+    # the reference's compiled wrapper
+    compiled = paged_cache._compiled_flex_attention
     paged_cache._compiled_flex_attention = flex_attention
+    try:
+        return _reference_cpu_steps(which, steps, warmup, budget_s, paged_cache, Cache,
+                                    compute_rope_params, apply_rope)
+    finally:
+        paged_cache._compiled_flex_attention = compiled
+
+
+def _reference_cpu_steps(which, steps, warmup, budget_s, paged_cache, Cache, compute_rope_params,
+                         apply_rope):
+    """The timed loop of ``reference_cpu_path`` (eager FlexAttention already in place)."""
+    import random
+
+    import torch
+
     threads = cpu_threads()
     torch.set_num_threads(threads)
     spec = REF_CPU_WORKLOADS[which]

@@ -45,3 +45,24 @@ def test_longdecode_defaults_to_config5_steps():
         assert bench.parse_args().steps == 2000
     finally:
         sys.argv = old
+
+
+def test_reference_cpu_path_puts_the_compiled_wrapper_back():
+    """The CPU timing swaps the reference module's compiled FlexAttention for the eager one;
+    the GPU comparisons that run later in the same bench process must see the compiled
+    wrapper again (the eager path scores the whole pool: slower, and out of memory on long
+    prefixes)."""
+    import pytest
+
+    if not os.path.isdir(os.path.join(ROOT, "baseline", "_ref", "hayate")):
+        pytest.skip("reference not installed in baseline/_ref")
+    sys.path.insert(0, ROOT)
+    import bench
+
+    mods, why = bench.import_reference()
+    assert mods is not None, why
+    paged_cache = mods[0]
+    before = paged_cache._compiled_flex_attention
+    out = bench.reference_cpu_path("config1", steps=1, warmup=0, budget_s=0.0)
+    assert out["kind"] == "reference" and out["value"] > 0
+    assert paged_cache._compiled_flex_attention is before
