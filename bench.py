@@ -23,8 +23,12 @@ timed steps are replayed from one CUDA graph captured from the same calls (no
 host launch inside the timed region); the same K steps launched one by one are
 timed beside it (`eager`), with per-launch events for the roofline.
 
+``--workload normrope`` times the fused QK-norm + RoPE + KV scatter kernel
+(``PagedKVBatch.prepare_layer``) on config 3's chunk.
+
 The default run adds, beside the config-2 headline: config 3 (and the same shape
-on longer prefixes), config 5 at every N (its own 128 steps, with each rank's
+on longer prefixes), the fused QK-norm + RoPE + scatter on config 3's chunk,
+config 5 at every N (its own 128 steps, with each rank's
 kernel time, host time and barrier wait), config 4's engine at N=1, the e2e
 number through the public API with host buffers, the CPU baseline, and at N=1
 the reference's own GPU attention (its torch.compile'd FlexAttention from
@@ -66,7 +70,8 @@ def parse_args():
                     help="timed steps (default 2000; config 5's 128 for --workload longdecode)")
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "prefill", "longdecode", "engine"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "prefill", "longdecode", "engine", "normrope"],
+                    default="decode")
     ap.add_argument("--split-tokens", type=int, default=0)
     ap.add_argument("--requests", type=int, default=64, help="decode requests per GPU (64 = config 2)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -87,7 +92,7 @@ def parse_args():
                     help="skip the reference's GPU path (timed beside ours by default at N=1)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = 128 if args.workload == "longdecode" else 2000
+        args.steps = {"longdecode": 128, "normrope": 200}.get(args.workload, 2000)
     return args
 
 
@@ -921,6 +926,80 @@ def run_prefill(args, world, rank, local, peaks, peak_kind, steps=None, warmup=N
     }
 
 
+def run_norm_rope(args, world, rank, local, peaks, peak_kind, steps: int = 50, warmup: int = 5):
+    """The fused QK-norm + RoPE + scatter kernel (``PagedKVBatch.prepare_layer``) on config
+    3's chunk: 8 requests x 512 new tokens on prefixes U[0, 4096]; q/k/v are the raw
+    projections ``[B, T, H, 128]`` the kernel normalises, rotates at their positions and
+    writes (q transposed, k/v into their pool pages). HBM-bound: per token it reads q, k, v
+    and that position's cos/sin rows and writes q, k, v once."""
+    import torch
+
+    from hayate_b200 import PagedKVCacheManager
+    from hayate_b200 import workloads as W
+
+    T = 512
+    prefixes = prefill_prefixes(2000 + rank, hi=4096)
+    pages = sum(math.ceil((n + T) / 128) for n in prefixes) + 8
+    manager = PagedKVCacheManager(1, 8, 128, pages * 128, 128, len(prefixes), torch.bfloat16, "cuda")
+    W.shuffle_free_pages(manager, 2000 + rank)
+    handles = []
+    for n in prefixes:
+        h = manager.allocate()
+        manager.reserve(h, n)
+        h.length = n
+        handles.append(h)
+    gen = torch.Generator(device="cuda").manual_seed(3000 + rank)
+    B = len(prefixes)
+    q = torch.randn(B, T, 32, 128, generator=gen, device="cuda").to(torch.bfloat16)
+    k = torch.randn(B, T, 8, 128, generator=gen, device="cuda").to(torch.bfloat16)
+    v = torch.randn(B, T, 8, 128, generator=gen, device="cuda").to(torch.bfloat16)
+    wq = (1 + 0.1 * torch.randn(128, generator=gen, device="cuda")).to(torch.bfloat16)
+    wk = (1 + 0.1 * torch.randn(128, generator=gen, device="cuda")).to(torch.bfloat16)
+    cos, sin = W.rope_angles(torch.arange(max(prefixes) + T, device="cuda"), 128)
+    cos, sin = cos.contiguous(), sin.contiguous()
+    batch = manager.begin_batch(handles, T)
+    tokens = B * T
+    # bytes per launch: q read + written (32 heads), k and v read + written (8 heads each),
+    # each token's cos and sin rows (fp32) read once
+    step_bytes = tokens * (2 * 32 * 128 * 2 + 4 * 8 * 128 * 2 + 2 * 128 * 4)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")  # > 126 MB L2
+
+    def step():
+        return batch.prepare_layer(0, q, k, v, wq, wk, cos, sin)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    manager.check_device_errors()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    with ClockSampler(local) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        for i in range(steps):
+            flush.fill_(i & 0xFF)  # evict the step's inputs from L2 (outside the timed events)
+            evs[i][0].record()
+            step()
+            evs[i][1].record()
+        torch.cuda.synchronize()
+        barrier(world)
+        clocks.hold(step)
+    manager.check_device_errors()
+    ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in evs) / steps, world)
+    achieved = step_bytes / (ms / 1e3) / 1e9
+    return {
+        "workload": "config 3's chunk (8 requests x 512 tokens on prefixes U[0, 4096]): fused QK-norm + "
+                    "RoPE + KV scatter of one layer (PagedKVBatch.prepare_layer)",
+        "value": round(achieved * world, 1), "unit": "GB/s", "ms_per_launch": round(ms, 4),
+        "bytes_per_launch": step_bytes,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "peak_source": f"{peak_kind} hbm_gbs", "kernel": "norm_rope_scatter_kernel"},
+        "l2": "256 MB buffer written between timed launches (L2 flush); events bracket each launch",
+        "gpu_launches": steps,
+        "clocks": clocks.summary(),
+    }
+
+
 # ---------------------------------------------------------------------------- long decode (cfg 5)
 LONG_GROUPS, LONG_PER_GROUP, LONG_PREFIX, LONG_CONTEXT, LONG_STEPS = 32, 16, 4096, 32768, 128
 
@@ -1367,6 +1446,9 @@ def main():
             # heaviest in two)
             result["prefill_long_prefix"] = run_prefill(args, world, rank, local, peaks, peak_kind,
                                                         steps=20, warmup=3, prefix_max=32768)
+            # the fused QK-norm + RoPE + scatter kernel (the caller's side of the path) on
+            # config 3's chunk
+            result["norm_rope"] = run_norm_rope(args, world, rank, local, peaks, peak_kind)
             # config 5 at every N: the request-partitioned long-context decode the 1/2/4/8-GPU
             # tok/s is quoted on (its own 128 steps, whatever --steps says)
             torch.cuda.empty_cache()
@@ -1377,6 +1459,9 @@ def main():
                 result["engine"] = engine_leg(args)
     elif args.workload == "prefill":
         result = run_prefill(args, world, rank, local, peaks, peak_kind)
+    elif args.workload == "normrope":
+        result = run_norm_rope(args, world, rank, local, peaks, peak_kind, steps=args.steps,
+                               warmup=args.warmup)
     else:
         result = run_longdecode(args, world, rank, local, peaks, peak_kind)
     if rank == 0:
