@@ -558,6 +558,27 @@ int decode_scratch_address(cudaStream_t stream, void** out) {
   return HYT_OK;
 }
 
+// The fused norm/RoPE/scatter kernels move 16 bytes per lane (8 features of a 16-bit row, 4
+// of an fp32 one) between global memory and registers or shared memory: every row they
+// read or write must start on a 16-byte boundary.
+int check_norm_rope_alignment(int dtype, const void* q, const void* k, const void* v, const void* q_out,
+                              const int64_t* qkv_strides, int n_qkv, const int64_t* q_out_strides,
+                              int n_out, const void* q_norm_weight, const void* k_norm_weight,
+                              const void* k_pool, const void* v_pool, const float* cos, const float* sin) {
+  const int per16 = 16 / elem_bytes(dtype);  // elements in 16 bytes
+  const void* ptrs[8] = {q, k, v, q_out, q_norm_weight, k_norm_weight, k_pool, v_pool};
+  for (const void* ptr : ptrs)
+    if (reinterpret_cast<uintptr_t>(ptr) % 16)
+      return fail(HYT_ERR_INVALID, "q/k/v/q_out, the norm weights and the pools must be 16-byte aligned");
+  for (int i = 0; i < n_qkv; ++i)
+    if (qkv_strides[i] % per16) return fail(HYT_ERR_INVALID, "q/k/v strides must be multiples of 16 bytes");
+  for (int i = 0; i < n_out; ++i)
+    if (q_out_strides[i] % per16) return fail(HYT_ERR_INVALID, "q_out strides must be multiples of 16 bytes");
+  if (reinterpret_cast<uintptr_t>(cos) % 16 || reinterpret_cast<uintptr_t>(sin) % 16)
+    return fail(HYT_ERR_INVALID, "cos/sin tables must be 16-byte aligned");
+  return HYT_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -629,16 +650,9 @@ int hyt_norm_rope_scatter(const void* q, const void* k, const void* v, const int
   if (rc != HYT_OK) return rc;
   if (head_dim != 128) return fail(HYT_ERR_UNSUPPORTED, "fused norm/RoPE/scatter needs head_dim 128");
   if (rope_positions < 1) return fail(HYT_ERR_INVALID, "rope_positions must be positive");
-  const int eb = elem_bytes(dtype);
-  const void* rows[4] = {q, k, v, q_out};
-  for (const void* r : rows)
-    if (reinterpret_cast<uintptr_t>(r) % (4 * eb)) return fail(HYT_ERR_INVALID, "q/k/v/q_out must be aligned to 4 elements");
-  for (int i = 0; i < 9; ++i)
-    if (qkv_strides[i] % 4) return fail(HYT_ERR_INVALID, "q/k/v strides must be multiples of 4 elements");
-  for (int i = 0; i < 3; ++i)
-    if (q_out_strides[i] % 4) return fail(HYT_ERR_INVALID, "q_out strides must be multiples of 4 elements");
-  if (reinterpret_cast<uintptr_t>(cos) % 16 || reinterpret_cast<uintptr_t>(sin) % 16)
-    return fail(HYT_ERR_INVALID, "cos/sin tables must be 16-byte aligned");
+  rc = check_norm_rope_alignment(dtype, q, k, v, q_out, qkv_strides, 9, q_out_strides, 3,
+                                 q_norm_weight, k_norm_weight, k_pool, v_pool, cos, sin);
+  if (rc != HYT_OK) return rc;
   hyt::NormRopeParams p;
   p.q = q;
   p.q_sb = qkv_strides[0]; p.q_st = qkv_strides[1]; p.q_sh = qkv_strides[2];
@@ -931,16 +945,9 @@ int hyt_norm_rope_scatter_packed(const void* q, const void* k, const void* v,
   if (rc != HYT_OK) return rc;
   if (head_dim != 128) return fail(HYT_ERR_UNSUPPORTED, "fused norm/RoPE/scatter needs head_dim 128");
   if (rope_positions < 1) return fail(HYT_ERR_INVALID, "rope_positions must be positive");
-  const int eb = elem_bytes(dtype);
-  const void* rows[4] = {q, k, v, q_out};
-  for (const void* r : rows)
-    if (reinterpret_cast<uintptr_t>(r) % (4 * eb)) return fail(HYT_ERR_INVALID, "q/k/v/q_out must be aligned to 4 elements");
-  for (int i = 0; i < 6; ++i)
-    if (qkv_strides[i] % 4) return fail(HYT_ERR_INVALID, "q/k/v strides must be multiples of 4 elements");
-  for (int i = 0; i < 2; ++i)
-    if (q_out_strides[i] % 4) return fail(HYT_ERR_INVALID, "q_out strides must be multiples of 4 elements");
-  if (reinterpret_cast<uintptr_t>(cos) % 16 || reinterpret_cast<uintptr_t>(sin) % 16)
-    return fail(HYT_ERR_INVALID, "cos/sin tables must be 16-byte aligned");
+  rc = check_norm_rope_alignment(dtype, q, k, v, q_out, qkv_strides, 6, q_out_strides, 2,
+                                 q_norm_weight, k_norm_weight, k_pool, v_pool, cos, sin);
+  if (rc != HYT_OK) return rc;
   hyt::NormRopeParams p;
   p.q = q;
   p.q_sb = 0; p.q_st = qkv_strides[0]; p.q_sh = qkv_strides[1];

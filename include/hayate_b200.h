@@ -184,6 +184,9 @@ int hyt_prefill_attention(const void* q, const int64_t* q_strides, const void* k
  * projections before the transpose: q [B, T, H_q, 128], k/v [B, T, H_kv, 128] with
  * element strides {b, t, h} (qkv_strides = q's 3, then k's, then v's). q_out is
  * [B, H_q, T, 128] with strides {b, h, t}. cos/sin are [rope_positions, 128] fp32.
+ * Every row starts on a 16-byte boundary: q, k, v, q_out, both norm weights, both pools
+ * and cos/sin 16-byte aligned, all strides multiples of 16 bytes (HYT_ERR_INVALID
+ * otherwise).
  */
 int hyt_norm_rope_scatter(const void* q, const void* k, const void* v, const int64_t* qkv_strides,
                           const void* q_norm_weight, const void* k_norm_weight, float eps,

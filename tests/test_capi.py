@@ -264,3 +264,33 @@ def test_prefill_plan_and_self_test_reject_bad_arguments():
     assert lib.hyt_prefill_plan(lens, None, 2, 64, 32, 0, 8, 0.0, 0.0, items, 4, ctypes.byref(n)) == -1
     assert lib.hyt_wait_self_test(None, None, None) == -1
     assert "null" in lib.hyt_last_error().decode()
+
+
+def _norm_rope_args(**overrides):
+    """hyt_norm_rope_scatter arguments for a shape it takes (16-byte aligned fake pointers:
+    nothing is dereferenced before the checks return)."""
+    qkv = _lib.int64_array([4 * 48 * 128, 48 * 128, 128] * 3)
+    outs = _lib.int64_array([32 * 4 * 128, 128, 32 * 128])
+    args = dict(q=16, k=16, v=16, qkv=qkv, wq=16, wk=16, eps=1e-6, cos=16, sin=16, positions=4096,
+                q_out=16, outs=outs, k_pool=16, v_pool=16, num_layers=1, layer=0, capacity=4096,
+                page_table=16, pts=32, cache_lens=16, batch=2, query_len=4, hq=32, hkv=8,
+                head_dim=128, page_size=128, dtype=0, err=None, stream=None)
+    args.update(overrides)
+    return list(args.values())
+
+
+@pytest.mark.parametrize("bad, message", [
+    (dict(q=24), "16-byte aligned"),        # 4-element (8-byte) aligned only
+    (dict(wk=8), "16-byte aligned"),
+    (dict(v_pool=40), "16-byte aligned"),
+    (dict(qkv=_lib.int64_array([4 * 48 * 128, 48 * 128 + 4, 128] * 3)), "multiples of 16 bytes"),
+    (dict(outs=_lib.int64_array([32 * 4 * 128, 132, 32 * 128])), "multiples of 16 bytes"),
+    (dict(cos=8), "16-byte aligned"),
+])
+def test_fused_norm_rope_refuses_rows_off_16_byte_boundaries(bad, message):
+    """The fused kernel moves 16 bytes per lane: a row that does not start on a 16-byte
+    boundary is refused on the host instead of reaching the GPU."""
+    lib = _lib.lib()
+    rc = lib.hyt_norm_rope_scatter(*_norm_rope_args(**bad))
+    assert rc == -1
+    assert message in lib.hyt_last_error().decode()
