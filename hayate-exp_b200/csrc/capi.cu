@@ -366,8 +366,9 @@ int launch_decode(const void* q, const int64_t* qs, const void* k_pool, const vo
                                        max_kv_len, split_tokens);
   if (L.max_splits > 65535) return fail(HYT_ERR_UNSUPPORTED, "too many splits for one launch");
   if (count > 65535 || g.num_kv_heads > 65535) return fail(HYT_ERR_UNSUPPORTED, "batch too large");
-  if (L.total > 0 && (workspace == nullptr || workspace_bytes < L.total))
-    return fail(HYT_ERR_WORKSPACE, "workspace missing or smaller than hyt_attention_workspace_bytes()");
+  if (L.total > 0 && (workspace == nullptr || workspace_bytes < L.total || reinterpret_cast<uintptr_t>(workspace) % 16))
+    return fail(HYT_ERR_WORKSPACE,
+                "workspace missing, not 16-byte aligned or smaller than hyt_attention_workspace_bytes()");
   CUtensorMap k_map, v_map;
   const int64_t planes = int64_t(g.num_layers) * g.num_kv_heads;
   int rc = pool_tensor_map(k_pool, g.dtype, g.head_dim, g.capacity, planes, 64, &k_map);
@@ -1082,8 +1083,10 @@ int hyt_paged_attention_packed_planned(
   if (num_items < 0 || num_splits < 0 || (num_items > 0 && items == nullptr))
     return fail(HYT_ERR_INVALID, "bad plan");
   if (num_items > 0 && num_splits > 0 &&
-      (plan_workspace == nullptr || plan_workspace_bytes < hyt_prefill_workspace_bytes(num_splits)))
-    return fail(HYT_ERR_WORKSPACE, "plan workspace missing or smaller than hyt_prefill_workspace_bytes()");
+      (plan_workspace == nullptr || plan_workspace_bytes < hyt_prefill_workspace_bytes(num_splits) ||
+       reinterpret_cast<uintptr_t>(plan_workspace) % 16))
+    return fail(HYT_ERR_WORKSPACE,
+                "plan workspace missing, not 16-byte aligned or smaller than hyt_prefill_workspace_bytes()");
   const hyt::PrefillPlan plan = make_prefill_plan(items, num_items, num_splits, plan_workspace);
   return packed_attention(q, q_strides, k_pool, v_pool, num_layers, layer, capacity_tokens,
                           page_table, page_table_stride, cache_lens, q_start, q_len, out,
@@ -1195,8 +1198,10 @@ int hyt_prefill_attention_planned(const void* q, const int64_t* q_strides, const
                 "query-head group and 16-byte aligned q/out rows");
   if (num_items < 0 || num_splits < 0 || (num_items > 0 && items == nullptr))
     return fail(HYT_ERR_INVALID, "bad plan");
-  if (num_splits > 0 && (workspace == nullptr || workspace_bytes < hyt_prefill_workspace_bytes(num_splits)))
-    return fail(HYT_ERR_WORKSPACE, "workspace missing or smaller than hyt_prefill_workspace_bytes()");
+  if (num_splits > 0 && (workspace == nullptr || workspace_bytes < hyt_prefill_workspace_bytes(num_splits) ||
+                         reinterpret_cast<uintptr_t>(workspace) % 16))
+    return fail(HYT_ERR_WORKSPACE,
+                "workspace missing, not 16-byte aligned or smaller than hyt_prefill_workspace_bytes()");
   if (num_items == 0)  // no plan: the default grid
     return launch_prefill(q, q_strides, k_pool, v_pool, g, page_table, cache_lens, out,
                           out_strides, scale, error_word, static_cast<cudaStream_t>(stream));

@@ -41,7 +41,7 @@ enum {
   HYT_ERR_INVALID = -1,     /* bad argument (null pointer, negative size, ...) */
   HYT_ERR_UNSUPPORTED = -2, /* valid but not served by this build (dtype/shape) */
   HYT_ERR_CUDA = -3,        /* a CUDA runtime/driver call failed */
-  HYT_ERR_WORKSPACE = -4    /* workspace missing or too small */
+  HYT_ERR_WORKSPACE = -4    /* workspace missing, too small or not 16-byte aligned */
 };
 
 enum { HYT_DTYPE_BF16 = 0, HYT_DTYPE_F16 = 1, HYT_DTYPE_F32 = 2 };
@@ -87,8 +87,8 @@ int hyt_kv_scatter(const void* k_new, const void* v_new, const int64_t* new_stri
  * head_dim 128, larger chunks) or the CUDA-core kernel (any other shape, f32).
  * q_strides/out_strides = {b, h, t} in elements. max_kv_len bounds
  * cache_lens[b] + query_len over the batch (sizes the split grid).
- * workspace: see hyt_attention_workspace_bytes; the counter area at its start
- * must be zero before the first use (hyt_workspace_init) and is left zero.
+ * workspace: see hyt_attention_workspace_bytes (16-byte aligned); the counter area at
+ * its start must be zero before the first use (hyt_workspace_init) and is left zero.
  */
 int hyt_paged_attention(const void* q, const int64_t* q_strides, const void* k_pool,
                         const void* v_pool, int32_t num_layers, int32_t layer,

@@ -225,6 +225,7 @@ def _planned_args(**overrides):
     (dict(items=None), -1, "bad plan"),
     (dict(num_splits=2), -4, "hyt_prefill_workspace_bytes"),
     (dict(num_splits=2, ws=16, ws_bytes=1024), -4, "hyt_prefill_workspace_bytes"),
+    (dict(num_splits=2, ws=8, ws_bytes=1 << 30), -4, "not 16-byte aligned"),
     (dict(head_dim=64), -2, "prefill kernel needs"),
 ])
 def test_planned_prefill_rejects_bad_arguments(bad, code, message):
