@@ -459,6 +459,52 @@ def test_fused_norm_rope_scatter_matches_unfused_path(query_len, dtype):
     assert (out0.float() - out1.float()).abs().max().item() <= 2e-2
 
 
+def test_fused_norm_rope_scatter_full_config3_chunk():
+    """The fused kernel on config 3's whole chunk (8 requests x 512 tokens over prefixes
+    U[0, 4096], shuffled pages): q against the unfused path, every written k/v row of the
+    chunk read back out of its page slot (v bit for bit: a copy), no other pool row touched."""
+    prefixes = [2998, 4045, 1590, 2020, 1436, 3762, 183, 2532]
+    T, dtype = 512, torch.bfloat16
+    gen = torch.Generator(device="cuda").manual_seed(33)
+    pages = sum(math.ceil((n + T) / 128) for n in prefixes) + 4
+    m = PagedKVCacheManager(1, 8, 128, pages * 128, 128, len(prefixes), dtype, "cuda")
+    W.shuffle_free_pages(m, 33)
+    hs = [m.allocate() for _ in prefixes]
+    for h, n in zip(hs, prefixes):
+        m.reserve(h, n)
+        h.length = n
+    B = len(prefixes)
+    q = torch.randn(B, T, 32, 128, generator=gen, device="cuda").to(dtype)
+    k = torch.randn(B, T, 8, 128, generator=gen, device="cuda").to(dtype)
+    v = torch.randn(B, T, 8, 128, generator=gen, device="cuda").to(dtype)
+    wq = (1 + 0.1 * torch.randn(128, generator=gen, device="cuda")).to(dtype)
+    wk = (1 + 0.1 * torch.randn(128, generator=gen, device="cuda")).to(dtype)
+    cos, sin = W.rope_angles(torch.arange(max(prefixes) + T, device="cuda"), 128)
+    cos, sin = cos.contiguous(), sin.contiguous()
+    positions = torch.tensor(prefixes, device="cuda")[:, None] + torch.arange(T, device="cuda")[None, :]
+    m.k_cache.fill_(7.0)
+    m.v_cache.fill_(7.0)
+    batch = m.begin_batch(hs, T)
+    q_fused = batch.prepare_layer(0, q, k, v, wq, wk, cos, sin)
+    torch.cuda.synchronize()
+    m.check_device_errors()
+    q_ref = reference_norm_rope(q, wq, cos, sin, positions)
+    k_ref = reference_norm_rope(k, wk, cos, sin, positions)
+    assert (q_fused.float() - q_ref.float()).abs().max().item() <= 2e-2
+    assert (q_fused == q_ref).float().mean().item() > 0.99
+    # the chunk's rows, gathered from their page slots
+    table = batch.page_table.long()
+    slots = table.gather(1, positions // 128) * 128 + positions % 128  # [B, T]
+    k_rows = m.k_cache[0, 0][:, slots]  # [H_kv, B, T, D]
+    v_rows = m.v_cache[0, 0][:, slots]
+    assert (k_rows.permute(1, 0, 2, 3).float() - k_ref.float()).abs().max().item() <= 2e-2
+    assert torch.equal(v_rows.permute(1, 2, 0, 3), v)
+    written = torch.zeros(m.k_cache.shape[3], dtype=torch.bool, device="cuda")
+    written[slots.reshape(-1)] = True
+    assert bool((m.k_cache[0, 0][:, ~written] == 7.0).all())
+    assert bool((m.v_cache[0, 0][:, ~written] == 7.0).all())
+
+
 @pytest.mark.parametrize("prefix, own, query_len", [(4096, 300, 1), (256, 1000, 1), (384, 130, 40)])
 def test_shared_prefix_pages_attend_like_private_copies(prefix, own, query_len):
     """Requests aliasing a prefix's pages (share) attend exactly like requests holding copies."""
