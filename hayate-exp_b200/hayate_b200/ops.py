@@ -147,6 +147,19 @@ def attention_workspace_bytes(batch: int, query_len: int, num_q_heads: int, num_
                                                         dtype_code(dtype)))
 
 
+def attention_counter_bytes(batch: int, num_kv_heads: int) -> int:
+    """Leading bytes of a split-KV decode workspace that hold the per-(request, KV head)
+    arrival counters: 4 bytes per unit, rounded up to 256 (the library's layout; pinned by
+    tests/test_capi.py). The kernels need them zero at launch and leave them zero."""
+    return -(-batch * num_kv_heads * 4 // 256) * 256
+
+
+def prefill_counter_bytes(num_splits: int) -> int:
+    """Leading bytes of a prefill-plan workspace that hold the split slots' counters (4 bytes
+    per slot, rounded up to 256; the library's layout, pinned by tests/test_capi.py)."""
+    return -(-num_splits * 4 // 256) * 256 if num_splits > 0 else 0
+
+
 def new_workspace(nbytes: int, device) -> torch.Tensor:
     """A zeroed byte workspace (the kernels keep its counter area zero between calls)."""
     return torch.zeros(max(nbytes, 1), dtype=torch.uint8, device=device)

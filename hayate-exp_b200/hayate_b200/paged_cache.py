@@ -472,6 +472,8 @@ class PagedKVCacheManager:
         self.prefill_plan = True       # schedule prefill launches (longest first, heaviest split)
         self.prefill_max_splits = 128  # split slots a schedule may use
         self._prefill_ws = None
+        self._prefill_ws_zero = 0  # leading bytes of the prefill workspace known to be zero
+        self._workspace_zero = 0   # leading bytes of the decode workspace known to be zero
         self._num_sms = None
 
     # ------------------------------------------------------------------ pages
@@ -764,8 +766,15 @@ class PagedKVCacheManager:
                                              self.split_tokens)
         if need == 0:
             return None
+        counters = ops.attention_counter_bytes(batch, self.num_kv_heads)
         if self._workspace is None or self._workspace.numel() < need:
             self._workspace = ops.new_workspace(need, self.device)
+        elif counters > self._workspace_zero:
+            # this layout's counters reach bytes an earlier, smaller layout used for partials
+            self._workspace[self._workspace_zero:counters].zero_()
+        # past this layout's counters the bytes may now hold partials; its counters are zero
+        # again after every launch
+        self._workspace_zero = counters
         return self._workspace
 
     @property
@@ -780,8 +789,14 @@ class PagedKVCacheManager:
         need = ops.prefill_workspace_bytes(num_splits)
         if need == 0:
             return None
+        counters = ops.prefill_counter_bytes(num_splits)
         if self._prefill_ws is None or self._prefill_ws.numel() < need:
             self._prefill_ws = ops.new_workspace(need, self.device)
+        elif counters > self._prefill_ws_zero:
+            # more split slots than any layout since the bytes were last known zero: the new
+            # counters cover bytes an earlier plan used for partials
+            self._prefill_ws[self._prefill_ws_zero:counters].zero_()
+        self._prefill_ws_zero = counters
         return self._prefill_ws
 
     def check_device_errors(self) -> None:

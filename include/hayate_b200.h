@@ -88,7 +88,10 @@ int hyt_kv_scatter(const void* k_new, const void* v_new, const int64_t* new_stri
  * q_strides/out_strides = {b, h, t} in elements. max_kv_len bounds
  * cache_lens[b] + query_len over the batch (sizes the split grid).
  * workspace: see hyt_attention_workspace_bytes (16-byte aligned); the counter area at
- * its start must be zero before the first use (hyt_workspace_init) and is left zero.
+ * its start (4 bytes per (request, KV head), rounded up to 256) must be zero when a call
+ * starts and is left zero. A buffer reused for a call with more (request, KV head) units
+ * than an earlier one must have the newly covered counter bytes zeroed first (they held
+ * that call's partials), or be zeroed whole (hyt_workspace_init).
  */
 int hyt_paged_attention(const void* q, const int64_t* q_strides, const void* k_pool,
                         const void* v_pool, int32_t num_layers, int32_t layer,
@@ -284,8 +287,10 @@ int32_t hyt_prefill_plan(const int32_t* cache_lens, const int32_t* q_lens, int32
                          int32_t max_splits, float item_overhead, float merge_cost,
                          int32_t* items, int32_t max_items, int32_t* num_splits);
 
-/* Workspace bytes a plan with num_splits split slots needs (its counters must be zero
- * before first use, hyt_workspace_init; the kernel leaves them zero). */
+/* Workspace bytes a plan with num_splits split slots needs (its counters, 4 bytes per
+ * slot rounded up to 256 at the start, must be zero before first use, hyt_workspace_init;
+ * the kernel leaves them zero; a buffer reused for a plan with more slots than an earlier
+ * one needs the newly covered counter bytes zeroed first). */
 size_t hyt_prefill_workspace_bytes(int32_t num_splits);
 
 /* hyt_prefill_attention launched on a plan from hyt_prefill_plan: items is the plan in

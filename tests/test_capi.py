@@ -295,3 +295,22 @@ def test_fused_norm_rope_refuses_rows_off_16_byte_boundaries(bad, message):
     rc = lib.hyt_norm_rope_scatter(*_norm_rope_args(**bad))
     assert rc == -1
     assert message in lib.hyt_last_error().decode()
+
+
+def test_workspace_counter_layout_matches_the_library():
+    """The Python managers zero only a workspace's counter bytes when a layout reaches past
+    the known-zero prefix; their counter sizes must be the library's layout."""
+    import torch
+
+    from hayate_b200 import ops
+
+    slot = 2 * (2 * 128 * 128 * 4 + 2 * 128 * 2 * 4)  # one prefill split slot's partials
+    for n in (1, 63, 64, 65, 200):
+        assert ops.prefill_workspace_bytes(n) == ops.prefill_counter_bytes(n) + n * slot
+    # decode: 4 splits of 1024 keys, 4 rows (32 query heads / 8 KV heads, one query)
+    for batch in (1, 7, 8, 9, 64, 100):
+        units, splits, rows = batch * 8, 4, 4
+        ml = -(-units * splits * rows * 2 * 4 // 256) * 256
+        o = units * splits * rows * 128 * 4
+        total = ops.attention_workspace_bytes(batch, 1, 32, 8, 128, 4096, torch.bfloat16, 1024)
+        assert total - ml - o == ops.attention_counter_bytes(batch, 8)

@@ -306,3 +306,30 @@ def test_copy_on_write_count_is_exact_when_all_holders_write():
     assert len(manager._free_pages) == 2
     manager.begin_batch([src, twin], 1)  # page 1 has 2 holders, both write: 1 copy
     assert len(manager._free_pages) == 1 and src.pages[1] != twin.pages[1]
+
+
+def test_shared_workspaces_zero_counters_a_new_layout_reaches():
+    """A grow-only workspace shared by layouts of different sizes: bytes a smaller layout
+    used for partials must be zero again before a larger layout uses them as counters."""
+    from hayate_b200 import ops
+
+    m = PagedKVCacheManager(1, 8, 128, 64 * 128, 128, 128, torch.bfloat16, "cpu")
+    m.split_tokens = 1024
+    big = m.workspace_for(100, 1, 32, 4096)  # allocates for 100 requests
+    big.fill_(0xFF)  # partials of the big layout (counters of a finished launch are zero...)
+    big[: ops.attention_counter_bytes(100, 8)] = 0  # ... as the kernels leave them
+    small = m.workspace_for(10, 1, 32, 4096)
+    assert small.data_ptr() == big.data_ptr()
+    small[ops.attention_counter_bytes(10, 8):] = 0xAB  # the small layout's partials
+    mid = m.workspace_for(60, 1, 32, 4096)
+    assert mid.data_ptr() == big.data_ptr()
+    assert int(mid[: ops.attention_counter_bytes(60, 8)].abs().sum()) == 0
+
+    pw = m.prefill_workspace(100)
+    pw.fill_(0xFF)
+    pw[: ops.prefill_counter_bytes(100)] = 0
+    pw2 = m.prefill_workspace(10)
+    pw2[ops.prefill_counter_bytes(10):] = 0xAB
+    pw3 = m.prefill_workspace(80)
+    assert pw3.data_ptr() == pw.data_ptr()
+    assert int(pw3[: ops.prefill_counter_bytes(80)].abs().sum()) == 0
